@@ -1,0 +1,71 @@
+// Host-side argument bundle shared by the C entry points and the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ccq {
+
+enum { LAMBDA_TOKEN = 0, LAMBDA_GATE = 1 };
+enum { DT_F32 = 0, DT_BF16 = 1, DT_F16 = 2 };
+
+struct CleanArgs {
+  int dtype, B, T, H, K, n_seqs;
+  const void* q;
+  const void* k;
+  int lambda_mode;
+  const void* lam;
+  const float* gate_w;
+  const float* gate_b;
+  float* lam_out;
+  const int64_t* cu_seqlens;
+  int position_offset, subtract_mean;
+  const float* initial_cov;
+  const float* initial_mean;
+  // forward outputs
+  void* q_clean;
+  float* final_cov;
+  float* final_mean;
+  // backward inputs / outputs
+  const float* state_cov;
+  const float* state_mean;
+  const void* dq_clean;
+  const float* dfinal_cov;
+  const float* dfinal_mean;
+  void* dq;
+  void* dk;
+  float* dlam;
+  float* dgate_w;
+  float* dgate_b;
+  float* dinitial_cov;
+  float* dinitial_mean;
+  // decode states
+  const float* cov_in;
+  const float* mean_in;
+  float* cov_out;
+  float* mean_out;
+  void* workspace;
+  size_t workspace_bytes;
+  cudaStream_t stream;
+};
+
+// Workspace carving: every region starts on a 256-byte boundary.
+inline size_t ws_align(size_t x) { return (x + 255) & ~size_t(255); }
+
+// SIMT path (any K <= 256, fp32/bf16/fp16)
+size_t simt_bwd_workspace(int B, int T, int H, int K, int n_seqs);
+cudaError_t simt_fwd(const CleanArgs& a, int* launches);
+cudaError_t simt_bwd(const CleanArgs& a, int* launches);
+
+// decode step (K % 4 == 0, K <= 256)
+cudaError_t decode_step(const CleanArgs& a, int* launches);
+
+// tensor-core path (bf16/fp16, K == 128)
+bool tc_supported(const CleanArgs& a, int op);
+size_t tc_fwd_workspace(int B, int T, int H, int K, int n_seqs);
+size_t tc_bwd_workspace(int B, int T, int H, int K, int n_seqs);
+cudaError_t tc_fwd(const CleanArgs& a, int* launches);
+cudaError_t tc_bwd(const CleanArgs& a, int* launches);
+
+}  // namespace ccq

@@ -1,0 +1,208 @@
+// C ABI of the B200 CCQ cleaning operator: argument validation, dispatch and error reporting.
+// Declarations and contracts: include/ccq_b200.h.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/ccq_b200.h"
+#include "args.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+thread_local int g_path = CCQ_PATH_NONE;
+thread_local int g_launches = 0;
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CCQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int check_common(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                 const void* lam, const float* gw, const float* gb, const int64_t* cu, int n_seqs) {
+  if (dtype != CCQ_F32 && dtype != CCQ_BF16 && dtype != CCQ_F16) return fail(CCQ_ERR_INVALID, "unknown dtype %d", dtype);
+  if (B < 1 || T < 0 || H < 1 || K < 1) return fail(CCQ_ERR_INVALID, "bad sizes B=%d T=%d H=%d K=%d", B, T, H, K);
+  if (K > 256) return fail(CCQ_ERR_UNSUPPORTED, "head size K=%d > 256 is not supported", K);
+  if ((int64_t)H * 65535 < 0 || H > 65535) return fail(CCQ_ERR_INVALID, "H=%d too large", H);
+  if (T > 0 && (q == nullptr || k == nullptr)) return fail(CCQ_ERR_INVALID, "q and k are required");
+  if (lambda_mode == CCQ_LAMBDA_TOKEN) {
+    if (T > 0 && lam == nullptr) return fail(CCQ_ERR_INVALID, "lambda (per token) is required");
+  } else if (lambda_mode == CCQ_LAMBDA_GATE) {
+    if (gw == nullptr || gb == nullptr) return fail(CCQ_ERR_INVALID, "gate_w and gate_b are required in GATE mode");
+  } else {
+    return fail(CCQ_ERR_INVALID, "unknown lambda_mode %d", lambda_mode);
+  }
+  if (cu == nullptr) {
+    if (n_seqs != B) return fail(CCQ_ERR_INVALID, "dense batch: n_seqs (%d) must equal B (%d)", n_seqs, B);
+  } else {
+    if (B != 1) return fail(CCQ_ERR_INVALID, "varlen batch (cu_seqlens given) needs B == 1, got %d", B);
+    if (n_seqs < 1) return fail(CCQ_ERR_INVALID, "varlen batch needs n_seqs >= 1");
+  }
+  if (n_seqs > 65535) return fail(CCQ_ERR_UNSUPPORTED, "n_seqs=%d > 65535", n_seqs);
+  return CCQ_OK;
+}
+
+ccq::CleanArgs base_args(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                         const void* lam, const float* gw, const float* gb, const int64_t* cu, int n_seqs,
+                         int position_offset, int subtract_mean, void* stream) {
+  ccq::CleanArgs a;
+  memset(&a, 0, sizeof(a));
+  a.dtype = dtype; a.B = B; a.T = T; a.H = H; a.K = K; a.n_seqs = n_seqs;
+  a.q = q; a.k = k;
+  a.lambda_mode = lambda_mode; a.lam = lam; a.gate_w = gw; a.gate_b = gb;
+  a.cu_seqlens = cu;
+  a.position_offset = position_offset;
+  a.subtract_mean = subtract_mean ? 1 : 0;
+  a.stream = (cudaStream_t)stream;
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ccq_last_error(void) { return g_err; }
+int ccq_last_path(void) { return g_path; }
+int ccq_last_launch_count(void) { return g_launches; }
+int ccq_version(void) { return 100; }
+
+size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_seqs) {
+  if (B < 1 || T < 0 || H < 1 || K < 1 || K > 256 || n_seqs < 1) return 0;
+  ccq::CleanArgs a;
+  memset(&a, 0, sizeof(a));
+  a.dtype = dtype; a.B = B; a.T = T; a.H = H; a.K = K; a.n_seqs = n_seqs;
+  if (op == CCQ_OP_FWD) {
+    return ccq::tc_supported(a, CCQ_OP_FWD) ? ccq::tc_fwd_workspace(B, T, H, K, n_seqs) : 0;
+  }
+  if (op == CCQ_OP_BWD) {
+    size_t s = ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
+    if (ccq::tc_supported(a, CCQ_OP_BWD)) {
+      size_t t = ccq::tc_bwd_workspace(B, T, H, K, n_seqs);
+      if (t > s) s = t;
+    }
+    return s;
+  }
+  return 0;
+}
+
+int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                  const void* lam, const float* gate_w, const float* gate_b, float* lam_out,
+                  const int64_t* cu_seqlens, int n_seqs, int position_offset, int subtract_mean,
+                  const float* initial_cov, const float* initial_mean, void* q_clean, float* final_cov,
+                  float* final_mean, void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  int st = check_common(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
+  if (st != CCQ_OK) return st;
+  if (T > 0 && q_clean == nullptr) return fail(CCQ_ERR_INVALID, "q_clean output is required");
+  ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                               position_offset, subtract_mean, stream);
+  a.lam_out = lambda_mode == CCQ_LAMBDA_GATE ? lam_out : nullptr;
+  a.initial_cov = initial_cov;
+  a.initial_mean = initial_mean;
+  a.q_clean = q_clean;
+  a.final_cov = final_cov;
+  a.final_mean = subtract_mean ? final_mean : nullptr;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  int launches = 0;
+  cudaError_t e;
+  if (ccq::tc_supported(a, CCQ_OP_FWD)) {
+    size_t need = ccq::tc_fwd_workspace(B, T, H, K, n_seqs);
+    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+      return fail(CCQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    e = ccq::tc_fwd(a, &launches);
+    g_path = CCQ_PATH_TCGEN05;
+  } else {
+    e = ccq::simt_fwd(a, &launches);
+    g_path = CCQ_PATH_SIMT;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_fwd launch");
+  g_launches = launches;
+  return CCQ_OK;
+}
+
+int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                  const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens, int n_seqs,
+                  int position_offset, int subtract_mean, const float* initial_cov, const float* initial_mean,
+                  const float* state_cov, const float* state_mean, const void* dq_clean,
+                  const float* dfinal_cov, const float* dfinal_mean, void* dq, void* dk, float* dlam,
+                  float* dgate_w, float* dgate_b, float* dinitial_cov, float* dinitial_mean, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  int st = check_common(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
+  if (st != CCQ_OK) return st;
+  if (T > 0 && (dq_clean == nullptr || dq == nullptr || dk == nullptr))
+    return fail(CCQ_ERR_INVALID, "dq_clean, dq and dk are required");
+  if (lambda_mode == CCQ_LAMBDA_GATE && (dgate_w == nullptr || dgate_b == nullptr))
+    return fail(CCQ_ERR_INVALID, "dgate_w and dgate_b are required in GATE mode");
+  ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                               position_offset, subtract_mean, stream);
+  a.initial_cov = initial_cov;
+  a.initial_mean = initial_mean;
+  a.state_cov = state_cov;
+  a.state_mean = state_mean;
+  a.dq_clean = dq_clean;
+  a.dfinal_cov = dfinal_cov;
+  a.dfinal_mean = dfinal_mean;
+  a.dq = dq;
+  a.dk = dk;
+  a.dlam = lambda_mode == CCQ_LAMBDA_TOKEN ? dlam : nullptr;
+  a.dgate_w = dgate_w;
+  a.dgate_b = dgate_b;
+  a.dinitial_cov = initial_cov ? dinitial_cov : nullptr;
+  a.dinitial_mean = (initial_mean && (subtract_mean || dfinal_mean)) ? dinitial_mean : nullptr;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  const bool tc = ccq::tc_supported(a, CCQ_OP_BWD) && state_cov != nullptr && (state_mean != nullptr || !subtract_mean);
+  const size_t need = tc ? ccq::tc_bwd_workspace(B, T, H, K, n_seqs) : ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
+  if (T > 0 && need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(CCQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  int launches = 0;
+  cudaError_t e;
+  if (tc) {
+    e = ccq::tc_bwd(a, &launches);
+    g_path = CCQ_PATH_TCGEN05;
+  } else {
+    e = ccq::simt_bwd(a, &launches);
+    g_path = CCQ_PATH_SIMT;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd launch");
+  g_launches = launches;
+  return CCQ_OK;
+}
+
+int ccq_decode_step(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                    const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens, int n_seqs,
+                    int position_offset, int subtract_mean, const float* cov_in, const float* mean_in,
+                    float* cov_out, float* mean_out, void* q_clean, void* stream) {
+  g_err[0] = 0;
+  int st = check_common(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
+  if (st != CCQ_OK) return st;
+  if (K % 4 != 0) return fail(CCQ_ERR_UNSUPPORTED, "decode step needs K %% 4 == 0, got K=%d", K);
+  if (cov_out == nullptr) return fail(CCQ_ERR_INVALID, "cov_out is required");
+  if (T > 0 && q_clean == nullptr) return fail(CCQ_ERR_INVALID, "q_clean output is required");
+  if (((uintptr_t)cov_out | (uintptr_t)cov_in) & 15)
+    return fail(CCQ_ERR_INVALID, "cov_in / cov_out must be 16-byte aligned");
+  ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                               position_offset, subtract_mean, stream);
+  a.cov_in = cov_in;
+  a.mean_in = mean_in;
+  a.cov_out = cov_out;
+  a.mean_out = mean_out;
+  a.q_clean = q_clean;
+  int launches = 0;
+  cudaError_t e = ccq::decode_step(a, &launches);
+  if (e != cudaSuccess) return cuda_fail(e, "ccq_decode_step launch");
+  g_path = CCQ_PATH_DECODE;
+  g_launches = launches;
+  return CCQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+/*
+ * ccq_b200.h -- C ABI of the B200-native CCQ cleaning operator.
+ *
+ * The operator (ledong0110/CCQ, ccq/ops/common/fused_read.py:11-25):
+ *
+ *   C_t = C_0 + sum_{j<=t} k_j k_j^T        m_t = m_0 + sum_{j<=t} k_j
+ *   pos_t = t + position_offset (1-based, clamped >= 1, restarting per document)
+ *   z_t[v] = sum_k q_t[k] C_t[k,v]          s_t = m_t . q_t
+ *   q_clean_t = q_t - lambda_t (z_t / pos_t - s_t m_t / pos_t^2)   (mean term iff subtract_mean)
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are DEVICE pointers unless stated; all tensors are contiguous.
+ *   - Token tensors (q, k, q_clean, dq, dk, ...) are [B, T, H, K] row-major in the activation
+ *     dtype.  Varlen batches use B == 1 and cu_seqlens (int64, [n_seqs + 1], device), exactly as
+ *     the reference's cu_seqlens argument; dense batches pass cu_seqlens = NULL and n_seqs = B.
+ *   - States are fp32: cov [n_seqs, H, K, K] in the fla layout (z = q @ C), mean [n_seqs, H, K].
+ *   - lambda is per token [B, T, H] in the activation dtype (CCQ_LAMBDA_TOKEN), or the per-head
+ *     gate lambda = sigmoid(W[h] . q_t + b[h]) with W [H, K] fp32 and b [H] fp32 computed inside
+ *     the kernels (CCQ_LAMBDA_GATE).
+ *   - stream is a cudaStream_t passed as void*; every launch goes to that stream, no entry point
+ *     synchronises, and none allocates device memory: the caller owns every buffer, including the
+ *     workspace sized by ccq_workspace_size().
+ *   - Every entry point returns a ccq_status; on failure ccq_last_error() returns a message for
+ *     the calling thread.  Calls on different streams from different threads are independent.
+ */
+#ifndef CCQ_B200_H_
+#define CCQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  CCQ_OK = 0,
+  CCQ_ERR_INVALID = 1,      /* bad pointer, shape, dtype or option */
+  CCQ_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement (e.g. K > 256) */
+  CCQ_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
+  CCQ_ERR_WORKSPACE = 4     /* workspace missing or smaller than ccq_workspace_size() */
+} ccq_status;
+
+typedef enum { CCQ_F32 = 0, CCQ_BF16 = 1, CCQ_F16 = 2 } ccq_dtype;
+
+typedef enum { CCQ_LAMBDA_TOKEN = 0, CCQ_LAMBDA_GATE = 1 } ccq_lambda_mode;
+
+typedef enum { CCQ_OP_FWD = 0, CCQ_OP_BWD = 1, CCQ_OP_DECODE = 2 } ccq_op;
+
+/* Implementation a call took (for tests and benchmarks): see ccq_last_path(). */
+typedef enum { CCQ_PATH_NONE = 0, CCQ_PATH_SIMT = 1, CCQ_PATH_TCGEN05 = 2, CCQ_PATH_DECODE = 3 } ccq_path;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ccq_last_error(void);
+
+/* Which kernel family the last successful call on this thread launched. */
+int ccq_last_path(void);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int ccq_version(void);
+
+/* Number of kernel launches the last successful call on this thread issued. */
+int ccq_last_launch_count(void);
+
+/*
+ * Bytes of workspace `op` needs for these sizes (0 if none).  total_tokens = B*T.
+ * Replaces the temporaries the reference allocates inside _fused_read_fwd/_fused_read_bwd
+ * (fused_read.py:385-394, :413-434).
+ */
+size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_seqs);
+
+/*
+ * Forward: q_clean, and optionally the final cov / mean states.
+ * Replaces FusedCCQCleanRead.forward / _fused_read_fwd (fused_read.py:379-403, :480-491).
+ *   lambda_mode == CCQ_LAMBDA_TOKEN: lam [B,T,H] activation dtype; gate_w/gate_b unused.
+ *   lambda_mode == CCQ_LAMBDA_GATE : gate_w [H,K] f32, gate_b [H] f32; lam unused.
+ *   lam_out: optional [B,T,H] f32, receives the lambda used (GATE mode only).
+ *   initial_cov / initial_mean: optional; initial_mean is ignored unless subtract_mean.
+ *   final_cov / final_mean: optional outputs (the backward's tensor-core path reads them back).
+ */
+int ccq_clean_fwd(int dtype, int B, int T, int H, int K,
+                  const void* q, const void* k,
+                  int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                  float* lam_out,
+                  const int64_t* cu_seqlens, int n_seqs,
+                  int position_offset, int subtract_mean,
+                  const float* initial_cov, const float* initial_mean,
+                  void* q_clean, float* final_cov, float* final_mean,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward: dq, dk, dlambda (TOKEN mode) or dW/db (GATE mode), and the initial-state gradients.
+ * Replaces FusedCCQCleanRead.backward / _fused_read_bwd (fused_read.py:406-460, :496-514).
+ *   state_cov / state_mean: the final states the forward wrote for these inputs (required when
+ *     the tensor-core path runs; pass NULL to let the library re-derive them, which costs an
+ *     extra pass over k).
+ *   dq_clean: upstream gradient [B,T,H,K]; dfinal_cov / dfinal_mean: optional state gradients.
+ *   dlam: [B,T,H] f32 output (TOKEN mode), may be NULL when lambda needs no gradient.
+ *   dgate_w [H,K] / dgate_b [H] f32 outputs (GATE mode; overwritten, summed over the batch).
+ *   dinitial_cov [n_seqs,H,K,K], dinitial_mean [n_seqs,H,K]: optional outputs; dinitial_mean is
+ *     written only when subtract_mean or dfinal_mean is given (fused_read.py:444-450).
+ */
+int ccq_clean_bwd(int dtype, int B, int T, int H, int K,
+                  const void* q, const void* k,
+                  int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                  const int64_t* cu_seqlens, int n_seqs,
+                  int position_offset, int subtract_mean,
+                  const float* initial_cov, const float* initial_mean,
+                  const float* state_cov, const float* state_mean,
+                  const void* dq_clean, const float* dfinal_cov, const float* dfinal_mean,
+                  void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
+                  float* dinitial_cov, float* dinitial_mean,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Recurrent (decode / short prefill) cleaning with the generation cache.
+ * Replaces fla fused_recurrent_gla(q, k, v=k, scale=1) + _CCQCleanQ as called by
+ * fused_ccq_clean(use_chunk=False) (ccq/ops/ccq_gdn/fused_clean.py:34-83) and
+ * ccq/ops/ccq_gla/fused_recurrent.py:26-38.  The state read is inclusive of the token.
+ *   cov_in / mean_in: cache states before the call (NULL = zeros); cov_out / mean_out: states
+ *   after the last token (may alias cov_in / mean_in for an in-place cache update).
+ *   mean_in/mean_out are used only when subtract_mean.
+ */
+int ccq_decode_step(int dtype, int B, int T, int H, int K,
+                    const void* q, const void* k,
+                    int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                    const int64_t* cu_seqlens, int n_seqs,
+                    int position_offset, int subtract_mean,
+                    const float* cov_in, const float* mean_in,
+                    float* cov_out, float* mean_out,
+                    void* q_clean, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CCQ_B200_H_ */
