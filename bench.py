@@ -196,8 +196,8 @@ def run_ours(args, rank, world, local_rank):
     def fwd():
         return ops.clean_fwd_raw(q, k, None, W, bias, 0, None, None, True, None, N)
 
-    def bwd(fc, fm):
-        return ops.clean_bwd_raw(q, k, None, W, bias, 0, None, None, True, None, N, fc, fm, dqc, None, None)
+    def bwd(fc, fm, aux):
+        return ops.clean_bwd_raw(q, k, None, W, bias, 0, None, None, True, None, N, fc, fm, aux, dqc, None, None)
 
     def allreduce(dW, db):
         if world > 1:
@@ -206,8 +206,8 @@ def run_ours(args, rank, world, local_rank):
 
     stream = torch.cuda.current_stream(device)
     for _ in range(args.warmup):
-        qc, fc, fm, _ = fwd()
-        dq, dk, (dW, db), _, _ = bwd(fc, fm)
+        qc, fc, fm, aux = fwd()
+        dq, dk, (dW, db), _, _ = bwd(fc, fm, aux)
         allreduce(dW, db)
     path_fwd = path_bwd = None
     n_launch = 0
@@ -223,12 +223,12 @@ def run_ours(args, rank, world, local_rank):
         for i in range(args.steps):
             e0, e1, e2 = ev[i]
             e0.record(stream)
-            qc, fc, fm, _ = fwd()
+            qc, fc, fm, aux = fwd()
             if path_fwd is None:
                 path_fwd = _lib.last_path()
             n_launch += _lib.last_launch_count()
             e1.record(stream)
-            dq, dk, (dW, db), _, _ = bwd(fc, fm)
+            dq, dk, (dW, db), _, _ = bwd(fc, fm, aux)
             if path_bwd is None:
                 path_bwd = _lib.last_path()
             n_launch += _lib.last_launch_count()

@@ -34,7 +34,7 @@ _SIGS = {
     'ccq_clean_fwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P,
                            _P, _SZ, _P]),
     'ccq_clean_bwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P,
-                           _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+                           _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     'ccq_decode_step': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
 }
 

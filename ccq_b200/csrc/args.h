@@ -18,7 +18,7 @@ struct CleanArgs {
   const void* lam;
   const float* gate_w;
   const float* gate_b;
-  float* lam_out;
+  float* token_aux;        // fwd output [B,T,H,2]: lambda_t, s_t
   const int64_t* cu_seqlens;
   int position_offset, subtract_mean;
   const float* initial_cov;
@@ -30,6 +30,7 @@ struct CleanArgs {
   // backward inputs / outputs
   const float* state_cov;
   const float* state_mean;
+  const float* token_aux_in;  // bwd input, as written by the forward
   const void* dq_clean;
   const float* dfinal_cov;
   const float* dfinal_mean;

@@ -93,7 +93,7 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
 }
 
 int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
-                  const void* lam, const float* gate_w, const float* gate_b, float* lam_out,
+                  const void* lam, const float* gate_w, const float* gate_b, float* token_aux,
                   const int64_t* cu_seqlens, int n_seqs, int position_offset, int subtract_mean,
                   const float* initial_cov, const float* initial_mean, void* q_clean, float* final_cov,
                   float* final_mean, void* workspace, size_t workspace_bytes, void* stream) {
@@ -103,7 +103,7 @@ int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   if (T > 0 && q_clean == nullptr) return fail(CCQ_ERR_INVALID, "q_clean output is required");
   ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
                                position_offset, subtract_mean, stream);
-  a.lam_out = lambda_mode == CCQ_LAMBDA_GATE ? lam_out : nullptr;
+  a.token_aux = token_aux;
   a.initial_cov = initial_cov;
   a.initial_mean = initial_mean;
   a.q_clean = q_clean;
@@ -131,7 +131,7 @@ int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const vo
 int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
                   const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens, int n_seqs,
                   int position_offset, int subtract_mean, const float* initial_cov, const float* initial_mean,
-                  const float* state_cov, const float* state_mean, const void* dq_clean,
+                  const float* state_cov, const float* state_mean, const float* token_aux, const void* dq_clean,
                   const float* dfinal_cov, const float* dfinal_mean, void* dq, void* dk, float* dlam,
                   float* dgate_w, float* dgate_b, float* dinitial_cov, float* dinitial_mean, void* workspace,
                   size_t workspace_bytes, void* stream) {
@@ -148,6 +148,7 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   a.initial_mean = initial_mean;
   a.state_cov = state_cov;
   a.state_mean = state_mean;
+  a.token_aux_in = token_aux;
   a.dq_clean = dq_clean;
   a.dfinal_cov = dfinal_cov;
   a.dfinal_mean = dfinal_mean;
@@ -160,7 +161,8 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   a.dinitial_mean = (initial_mean && (subtract_mean || dfinal_mean)) ? dinitial_mean : nullptr;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
-  const bool tc = ccq::tc_supported(a, CCQ_OP_BWD) && state_cov != nullptr && (state_mean != nullptr || !subtract_mean);
+  const bool tc = ccq::tc_supported(a, CCQ_OP_BWD) && state_cov != nullptr && token_aux != nullptr &&
+                  (state_mean != nullptr || !subtract_mean);
   const size_t need = tc ? ccq::tc_bwd_workspace(B, T, H, K, n_seqs) : ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
   if (T > 0 && need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(CCQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);

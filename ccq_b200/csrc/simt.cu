@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(CleanArgs a) {
     load_tile<Tin, BT, KP, QS>(s_q, q, sq, t0, h, H, K);
     load_tile<Tin, BT, KP, QS>(s_k, kp, sq, t0, h, H, K);
     __syncthreads();
-    chunk_scalars<Tin, BT, KP, QS>(a, sq, t0, h, s_q, s_w, gate_b, s_lam, s_ipos, vt == 0 ? a.lam_out : nullptr);
+    chunk_scalars<Tin, BT, KP, QS>(a, sq, t0, h, s_q, s_w, gate_b, s_lam, s_ipos, nullptr);
     {  // A = tril(q k^T)
       float acc[BT / 16][BT / 16];
       zero(acc);
@@ -147,6 +147,14 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(CleanArgs a) {
         }
     }
     __syncthreads();
+    if (a.token_aux && vt == 0) {
+      for (int t = tid; t < BT; t += NT)
+        if (t0 + t < sq.len) {
+          float* aux = a.token_aux + ((sq.bos + t0 + t) * H + h) * 2;
+          aux[0] = s_lam[t];
+          if (!a.subtract_mean) aux[1] = 0.f;
+        }
+    }
     if (a.subtract_mean) {
       // s_t = m_prev . q_t + sum_{j<=t} A[t][j];  s_sp = s_t / pos_t^2
       const int warp = tid >> 5, lane = tid & 31;
@@ -156,6 +164,8 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(CleanArgs a) {
         for (int j = lane; j < BT; j += 32) d += s_A[t * AS + j];
         d = warp_sum(d);
         if (lane == 0) s_sp[t] = d * s_ipos[t] * s_ipos[t];
+        if (lane == 0 && vt == 0 && a.token_aux && t0 + t < sq.len)
+          a.token_aux[((sq.bos + t0 + t) * H + h) * 2 + 1] = d;
       }
       // running key sum inside the chunk for this column tile
       for (int cc = tid; cc < VT; cc += NT) {

@@ -1,0 +1,520 @@
+// Tensor-core (tcgen05 / TMEM / TMA) forward of the CCQ cleaning operator, bf16 or fp16, K = 128.
+//
+// One CTA per (document, head) walks the document in chunks of BT = 128 tokens.  The covariance
+// state C (128 x 128 fp32) lives in TMEM for the whole document and is never written to HBM, so
+// the kernel reads q and k once and writes q_clean once.  Per chunk (Q, K = 128 x 128 tiles):
+//   F1  A  = Q [K ; m_hi ; m_lo ; w_hi ; w_lo]^T     (N = 144: q k_j^T, q.m_prev, and q.w for the gate)
+//   F3  C += K^T K                                   (the state update, fp32 accumulate in TMEM)
+//   F2a Z  = Q bf16(C_prev)
+//   F2b Z += P' K,  P'[t][j] = (A[t][j] - s_t / pos_t) [j <= t]
+// so that Z_t = z_t - (s_t / pos_t)(m_t - m_prev) and the epilogue only adds the rank-1 term:
+//   q_clean_t = q_t - (lambda_t / pos_t) (Z_t - (s_t / pos_t) m_prev)
+// which is the reference's q_t - lambda_t (z_t / pos_t - s_t m_t / pos_t^2)
+// (ccq/ops/common/fused_read.py:11-16, kernel at :86-174).
+//
+// Warp roles (384 threads): warp 0 issues TMA loads, warp 1 allocates TMEM and issues every MMA
+// from one thread, warps 2-3 ("aux") keep the running key sum m and patch the K tile's extra rows,
+// warps 4-11 ("epilogue", two warpgroups splitting the 128 columns) turn A into P', convert C to
+// the bf16 operand for the next chunk and write q_clean.  Every mbarrier wait is bounded; on a
+// timeout the CTA records an error in the workspace and unwinds.
+#include "args.h"
+#include "common.cuh"
+#include "tc_common.cuh"
+#include "tma_host.h"
+
+namespace ccq {
+
+namespace {
+using namespace tc;
+
+constexpr int F_THREADS = 384;
+constexpr int F_BT = 128;
+constexpr uint32_t F_QPANEL = 16384;                  // 128 rows x 128 B
+constexpr uint32_t F_QTILE = 2 * F_QPANEL;            // 128 x 128 bf16
+constexpr uint32_t F_KROWS = 144;                     // 128 keys + m_hi, m_lo, w_hi, w_lo, zeros
+constexpr uint32_t F_KPANEL = F_KROWS * 128;          // 18432
+constexpr uint32_t F_KTILE = 2 * F_KPANEL;
+constexpr uint32_t F_OFF_Q = 0;                       // two stages
+constexpr uint32_t F_OFF_K = 2 * F_QTILE;             // two stages
+constexpr uint32_t F_OFF_C = F_OFF_K + 2 * F_KTILE;   // bf16 C_prev (MN-major B operand)
+constexpr uint32_t F_OFF_P = F_OFF_C + F_QTILE;       // P' (K-major A operand)
+constexpr uint32_t F_OFF_SMALL = F_OFF_P + F_QTILE;   // 204800
+constexpr uint32_t T_C = 0, T_A = 128, T_Z = 272;      // TMEM columns: C (128), A (144), Z (128)
+
+struct FwdSmall {
+  float m_buf[2][128];
+  float s_part[2][128];
+  float lam[128], ipos[128], sp[128];
+  uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
+  uint64_t a_full, a_free, cconv, cprev_free, c_full, pready, z_full, z_free, mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t F_SMEM = F_OFF_SMALL + sizeof(FwdSmall) + 1024;
+static_assert(F_SMEM <= 232448, "forward kernel shared memory");
+
+__device__ __forceinline__ void nbar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// every thread of the named-barrier group gets the OR of v
+__device__ __forceinline__ bool nbar_any(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// 4 consecutive fp32 TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(taddr));
+  v[0] = __uint_as_float(r0);
+  v[1] = __uint_as_float(r1);
+  v[2] = __uint_as_float(r2);
+  v[3] = __uint_as_float(r3);
+}
+
+template <int AB16>
+__device__ __forceinline__ float act_load(const void* p, int64_t i) {
+  if (AB16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+template <int AB16>
+__device__ __forceinline__ uint32_t split_hi(float x, float* rest) {
+  if (AB16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(x);
+    *rest = x - __bfloat162float(h);
+    return (uint32_t)__bfloat16_as_ushort(h);
+  } else {
+    __half h = __float2half_rn(x);
+    *rest = x - __half2float(h);
+    return (uint32_t)__half_as_ushort(h);
+  }
+}
+template <int AB16>
+__device__ __forceinline__ uint32_t to16(float x) {
+  if (AB16) return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+  return (uint32_t)__half_as_ushort(__float2half_rn(x));
+}
+
+template <int AB16>
+__global__ void __launch_bounds__(F_THREADS, 1)
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, CleanArgs a,
+                  int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  FwdSmall& S = *reinterpret_cast<FwdSmall*>(sm + F_OFF_SMALL);
+  const uint32_t sbase = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.H;
+  const int h = blockIdx.x % H, n = blockIdx.x / H;
+  const Seq sq = seq_of(n, a.T, a.cu_seqlens);
+  const int nchunks = (sq.len + F_BT - 1) / F_BT;
+  const int64_t st_base = ((int64_t)n * H + h) * 128;
+  const bool sub_mean = a.subtract_mean != 0;
+  const bool gate = a.lambda_mode == LAMBDA_GATE;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.kready[i], 1);
+      mbar_init(&S.empty[i], 3);
+      mbar_init(&S.m_ready[i], 1);
+      mbar_init(&S.m_free[i], 1);
+    }
+    mbar_init(&S.a_full, 1);
+    mbar_init(&S.a_free, 1);
+    mbar_init(&S.cconv, 1);
+    mbar_init(&S.cprev_free, 1);
+    mbar_init(&S.c_full, 1);
+    mbar_init(&S.pready, 1);
+    mbar_init(&S.z_full, 1);
+    mbar_init(&S.z_free, 1);
+    mbar_init(&S.mma_done, 1);
+    S.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&S.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(&S.empty[s], ((c - 2) >> 1) & 1)) {
+          atomicOr(err, 1);
+          S.abort = 1;
+          break;
+        }
+        if (*(volatile int*)&S.abort) break;
+        mbar_arrive_expect_tx(&S.full[s], 2 * F_QTILE);
+        const int row = (int)(sq.bos + (int64_t)c * F_BT);
+        uint8_t* q_dst = sm + F_OFF_Q + s * F_QTILE;
+        uint8_t* k_dst = sm + F_OFF_K + s * F_KTILE;
+        tma_load_3d(q_dst, &tmq, &S.full[s], 0, h, row);
+        tma_load_3d(q_dst + F_QPANEL, &tmq, &S.full[s], 64, h, row);
+        tma_load_3d(k_dst, &tmk, &S.full[s], 0, h, row);
+        tma_load_3d(k_dst + F_KPANEL, &tmk, &S.full[s], 64, h, row);
+        ++issued;
+      }
+      // never leave the CTA with bulk copies in flight
+      for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) mbar_wait(&S.full[c & 1], (c >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_a = idesc_f16(128, 144, AB16, 0, 0);
+      const uint32_t id_z1 = idesc_f16(128, 128, AB16, 0, 1);
+      const uint32_t id_c = idesc_f16(128, 128, AB16, 1, 1);
+      const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c & 1;
+        const uint32_t sQ = sbase + F_OFF_Q + s * F_QTILE, sK = sbase + F_OFF_K + s * F_KTILE;
+        ok = mbar_wait(&S.kready[s], (c >> 1) & 1) && (c == 0 || mbar_wait(&S.a_free, (c - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_A, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
+               sdesc(sK + (ks >> 2) * F_KPANEL + (ks & 3) * 32, 16, 1024), id_a, ks > 0);
+        umma_commit(&S.a_full);
+        ok = mbar_wait(&S.cconv, c & 1);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_C, sdesc(sK + ks * 2048, F_KPANEL, 1024), sdesc(sK + ks * 2048, F_KPANEL, 1024), id_c, 1);
+        umma_commit(&S.c_full);
+        ok = (c == 0 || mbar_wait(&S.z_free, (c - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_Z, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
+               sdesc(sC + ks * 2048, F_QPANEL, 1024), id_z1, ks > 0);
+        umma_commit(&S.cprev_free);
+        ok = mbar_wait(&S.pready, c & 1);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_Z, sdesc(sP + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
+               sdesc(sK + ks * 2048, F_KPANEL, 1024), id_z1, 1);
+        umma_commit(&S.z_full);
+        umma_commit(&S.empty[s]);
+      }
+      if (!ok) {
+        atomicOr(err, 2);
+        S.abort = 1;
+      }
+      // TMEM is freed only after every issued MMA has completed
+      umma_commit(&S.mma_done);
+      mbar_wait(&S.mma_done, 0);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ aux: running key sum
+    const int at = threadIdx.x - 64;           // 0..63, owns dims 2at, 2at+1
+    const uint32_t p = at >> 5;                // panel
+    const uint32_t e = (2 * at) & 63;          // element inside the panel row
+    const uint32_t ch = e >> 3, cb = (e & 7) * 2;
+    float m0v = 0.f, m1v = 0.f;
+    if (sub_mean && a.initial_mean) {
+      m0v = a.initial_mean[st_base + 2 * at];
+      m1v = a.initial_mean[st_base + 2 * at + 1];
+    }
+    S.m_buf[0][2 * at] = m0v;
+    S.m_buf[0][2 * at + 1] = m1v;
+    uint32_t wh = 0, wl = 0;
+    if (gate) {
+      float r0, r1;
+      const uint32_t h0 = split_hi<AB16>(a.gate_w[(int64_t)h * 128 + 2 * at], &r0);
+      const uint32_t h1 = split_hi<AB16>(a.gate_w[(int64_t)h * 128 + 2 * at + 1], &r1);
+      wh = h0 | (h1 << 16);
+      wl = to16<AB16>(r0) | (to16<AB16>(r1) << 16);
+    }
+    for (int s = 0; s < 2; ++s) {
+      const uint32_t kb = sbase + F_OFF_K + s * F_KTILE + p * F_KPANEL;
+      for (uint32_t row = 130; row < F_KROWS; ++row)
+        st_shared_u32(kb + sw128(row, ch) + cb, row == 130 ? wh : (row == 131 ? wl : 0u));
+    }
+    nbar_sync(2, 64);
+    if (at == 0) mbar_arrive(&S.m_ready[0]);
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c & 1;
+      const bool ok = mbar_wait(&S.full[s], (c >> 1) & 1);
+      if (nbar_any(2, 64, !ok)) {
+        if (at == 0) { atomicOr(err, 4); S.abort = 1; }
+        break;
+      }
+      const uint32_t kt = sbase + F_OFF_K + s * F_KTILE;
+      const int valid = min(F_BT, sq.len - c * F_BT);
+      if (valid < F_BT) {  // keys past the end of the document belong to the next one: zero them
+        const uint32_t wp = at >> 5, wi = at & 31;
+        for (int rr = valid; rr < F_BT; ++rr) st_shared_u32(kt + wp * F_KPANEL + sw128(rr, wi >> 2) + (wi & 3) * 4, 0u);
+      }
+      {  // rows 128 / 129: m_prev split into two 16-bit parts
+        float r0, r1;
+        const uint32_t h0 = split_hi<AB16>(sub_mean ? m0v : 0.f, &r0);
+        const uint32_t h1 = split_hi<AB16>(sub_mean ? m1v : 0.f, &r1);
+        const uint32_t kb = kt + p * F_KPANEL;
+        st_shared_u32(kb + sw128(128, ch) + cb, h0 | (h1 << 16));
+        st_shared_u32(kb + sw128(129, ch) + cb, to16<AB16>(r0) | (to16<AB16>(r1) << 16));
+      }
+      fence_async_smem();
+      nbar_sync(2, 64);
+      if (at == 0) mbar_arrive(&S.kready[s]);
+      if (sub_mean) {
+        float acc0 = 0.f, acc1 = 0.f;
+        const uint32_t kb = kt + p * F_KPANEL + cb;
+#pragma unroll 8
+        for (int tt = 0; tt < F_BT; ++tt) {
+          const float2 f = unpack2<AB16>(ld_shared_u32(kb + sw128(tt, ch)));
+          acc0 += f.x;
+          acc1 += f.y;
+        }
+        m0v += acc0;
+        m1v += acc1;
+      }
+      bool ok2 = (c == 0) || mbar_wait(&S.m_free[(c - 1) & 1], ((c - 1) >> 1) & 1);
+      if (nbar_any(2, 64, !ok2)) {
+        if (at == 0) { atomicOr(err, 8); S.abort = 1; }
+        break;
+      }
+      S.m_buf[(c + 1) & 1][2 * at] = m0v;
+      S.m_buf[(c + 1) & 1][2 * at + 1] = m1v;
+      nbar_sync(2, 64);
+      if (at == 0) {
+        mbar_arrive(&S.m_ready[(c + 1) & 1]);
+        mbar_arrive(&S.empty[s]);
+      }
+    }
+    if (sub_mean && a.final_mean) {
+      a.final_mean[st_base + 2 * at] = m0v;
+      a.final_mean[st_base + 2 * at + 1] = m1v;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (256 threads)
+    const int et = threadIdx.x - 128;
+    const int g = et >> 7;                        // column half
+    const int qd = warp & 3;                      // TMEM lane quadrant of this warp
+    const int r = 32 * qd + lane;                 // token (A, Z) or state row (C)
+    const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
+    const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
+    const float gate_b = gate ? a.gate_b[h] : 0.f;
+    float v[64];
+    // initial state -> TMEM C and the bf16 operand for chunk 0
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int col0 = 64 * g + 32 * hf;
+      if (a.initial_cov) {
+        const float4* src = reinterpret_cast<const float4*>(a.initial_cov + (st_base + r) * 128 + col0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 f = src[i];
+          v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      tmem_st32(lrow + T_C + col0, v);
+      if (nchunks == 0 && a.final_cov) {
+        float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + col0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        st_shared_v4(sC + g * F_QPANEL + sw128(r, 4 * hf + cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
+                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
+                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+    }
+    tmem_st_wait();
+    fence_async_smem();
+    tc_fence_before();
+    nbar_sync(1, 256);
+    if (et == 0) mbar_arrive(&S.cconv);
+
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c & 1;
+      const int t0 = c * F_BT;
+      const int valid = min(F_BT, sq.len - t0);
+      const int t = r;
+      // ---------------- P' = (A - s/pos) on and below the diagonal
+      bool ok = mbar_wait(&S.a_full, c & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 16); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_A + 64 * g, v);
+      tmem_ld32(lrow + T_A + 64 * g + 32, v + 32);
+      float ext[4] = {0.f, 0.f, 0.f, 0.f};
+      if (g == 0) tmem_ld4(lrow + T_A + 128, ext);
+      const float ipos = 1.f / position_of(t0 + t, a.position_offset);
+      float part = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 64; ++jj) part += (64 * g + jj <= t) ? v[jj] : 0.f;
+      if (g == 0) {
+        part += ext[0] + ext[1];
+        float lamv;
+        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
+        else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
+        S.lam[t] = lamv;
+        S.ipos[t] = ipos;
+      }
+      S.s_part[g][t] = part;
+      nbar_sync(1, 256);
+      const float st = sub_mean ? S.s_part[0][t] + S.s_part[1][t] : 0.f;
+      const float sp = st * ipos;
+      if (g == 0) {
+        S.sp[t] = sp;
+        if (a.token_aux && t < valid) {
+          float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
+          *aux = make_float2(S.lam[t], st);
+        }
+      }
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const int j0 = 64 * g + 8 * cc + 2 * e2;
+          const float x0 = j0 <= t ? v[8 * cc + 2 * e2] - sp : 0.f;
+          const float x1 = j0 + 1 <= t ? v[8 * cc + 2 * e2 + 1] - sp : 0.f;
+          w[e2] = pack2<AB16>(x0, x1);
+        }
+        st_shared_v4(sP + g * F_QPANEL + sw128(t, cc), w[0], w[1], w[2], w[3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) {
+        mbar_arrive(&S.pready);
+        mbar_arrive(&S.a_free);
+      }
+      // ---------------- C after this chunk -> bf16 operand of the next chunk (or the final state)
+      ok = mbar_wait(&S.c_full, c & 1) && mbar_wait(&S.cprev_free, c & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 32); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_C + 64 * g, v);
+      tmem_ld32(lrow + T_C + 64 * g + 32, v + 32);
+      if (c + 1 < nchunks) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)
+          st_shared_v4(sC + g * F_QPANEL + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
+                       pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
+                       pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+        fence_async_smem();
+      } else if (a.final_cov) {
+        float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * g);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.cconv);
+      // ---------------- q_clean = q - lam/pos (Z - sp m_prev)
+      ok = mbar_wait(&S.z_full, c & 1) && mbar_wait(&S.m_ready[s], (c >> 1) & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 64); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_Z + 64 * g, v);
+      tmem_ld32(lrow + T_Z + 64 * g + 32, v + 32);
+      {
+        const float cf = S.lam[t] * S.ipos[t];
+        const float spv = S.sp[t];
+        const float* mp = S.m_buf[s] + 64 * g;
+        const uint32_t qrow = sbase + F_OFF_Q + s * F_QTILE + g * F_QPANEL;
+        void* orow = (uint8_t*)a.q_clean + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint4 qv = ld_shared_v4(qrow + sw128(t, cc));
+          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int jj = 8 * cc + 2 * e2;
+            const float2 qf = unpack2<AB16>(qw[e2]);
+            const float r0 = v[jj] - spv * mp[jj];
+            const float r1 = v[jj + 1] - spv * mp[jj + 1];
+            o[e2] = pack2<AB16>(qf.x - cf * r0, qf.y - cf * r1);
+          }
+          if (t < valid) reinterpret_cast<uint4*>(orow)[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) {
+        mbar_arrive(&S.z_free);
+        mbar_arrive(&S.m_free[s]);
+        mbar_arrive(&S.empty[s]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+template <int AB16>
+cudaError_t launch(const CleanArgs& a, int* launches) {
+  CUtensorMap tq, tk;
+  const int64_t rows = (int64_t)a.B * a.T;
+  cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, F_BT, AB16 != 0);
+  if (e != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
+  int* err = reinterpret_cast<int*>(a.workspace);
+  if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
+  auto kern = tc_fwd_kernel<AB16>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM)) != cudaSuccess)
+    return e;
+  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, a, err);
+  *launches += 1;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t tc_fwd_workspace(int, int, int, int, int) { return 256; }
+
+cudaError_t tc_fwd(const CleanArgs& a, int* launches) {
+  return a.dtype == DT_BF16 ? launch<1>(a, launches) : launch<0>(a, launches);
+}
+
+}  // namespace ccq

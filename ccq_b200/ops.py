@@ -11,6 +11,7 @@ There is no CPU or eager fallback: a missing library or a CPU tensor raises.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -93,6 +94,19 @@ def reduce_lambda_grad(dlam3, lam):
     return dl.to(lam.dtype)
 
 
+def _check_device_error(ws, what):
+    """With CCQ_B200_CHECK=1, synchronise and raise if the kernels flagged a bounded-wait timeout.
+
+    The tensor-core kernels write a non-zero word at the start of their workspace when one of
+    their pipeline waits gives up; normal calls leave it zero."""
+    if ws is None or os.environ.get('CCQ_B200_CHECK') != '1':
+        return
+    torch.cuda.synchronize(ws.device)
+    code = int(ws[:4].view(torch.int32).item())
+    if code:
+        raise _lib.CCQError(_lib.CCQ_ERR_CUDA, f'{what}: device pipeline timeout, code {code:#x}')
+
+
 def _workspace(op, dtype, B, T, H, K, N, device):
     nbytes = _lib.load().ccq_workspace_size(op, dtype, B, T, H, K, N)
     if nbytes == 0:
@@ -100,28 +114,28 @@ def _workspace(op, dtype, B, T, H, K, N, device):
     return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
 
 
-def clean_fwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N,
-                  want_lambda=False):
-    """One ccq_clean_fwd call; returns (q_clean, final_cov, final_mean, lambda_used or None)."""
+def clean_fwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N):
+    """One ccq_clean_fwd call; returns (q_clean, final_cov, final_mean, token_aux [B,T,H,2] fp32)."""
     B, T, H, K = q.shape
     dev = q.device
     dt = _dtype_code(q)
     qc = torch.empty_like(q)
     fcov = torch.empty(N, H, K, K, device=dev, dtype=torch.float32)
     fmean = torch.empty(N, H, K, device=dev, dtype=torch.float32) if subtract_mean else None
-    lam_out = torch.empty(B, T, H, device=dev, dtype=torch.float32) if (want_lambda and gate_w is not None) else None
+    aux = torch.empty(B, T, H, 2, device=dev, dtype=torch.float32)
     ws, nbytes = _workspace(_lib.CCQ_OP_FWD, dt, B, T, H, K, N, dev)
     mode = _lib.CCQ_LAMBDA_GATE if gate_w is not None else _lib.CCQ_LAMBDA_TOKEN
     lib = _lib.load()
     with torch.cuda.device(dev):
-        st = lib.ccq_clean_fwd(dt, B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(gate_w), _p(gate_b), _p(lam_out),
+        st = lib.ccq_clean_fwd(dt, B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(gate_w), _p(gate_b), _p(aux),
                                _p(cu), N, int(position_offset), int(bool(subtract_mean)), _p(h0), _p(m0),
                                _p(qc), _p(fcov), _p(fmean), _p(ws), nbytes, _stream(dev))
     _lib.check(st)
-    return qc, fcov, fmean, lam_out
+    _check_device_error(ws, 'ccq_clean_fwd')
+    return qc, fcov, fmean, aux
 
 
-def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N, fcov, fmean,
+def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N, fcov, fmean, aux,
                   dqc, dfinal_cov, dfinal_mean, want_dlam=True):
     """One ccq_clean_bwd call; returns (dq, dk, dlam3 | (dW, db), dh0, dm0)."""
     B, T, H, K = q.shape
@@ -142,9 +156,11 @@ def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_
     with torch.cuda.device(dev):
         st = lib.ccq_clean_bwd(dt, B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(gate_w), _p(gate_b), _p(cu), N,
                                int(position_offset), int(bool(subtract_mean)), _p(h0), _p(m0), _p(fcov),
-                               _p(fmean), _p(dqc), _p(dfinal_cov), _p(dfinal_mean), _p(dq), _p(dk), _p(dlam),
+                               _p(fmean), _p(aux), _p(dqc), _p(dfinal_cov), _p(dfinal_mean), _p(dq), _p(dk), _p(dlam),
                                _p(dW), _p(db), _p(dh0), _p(dm0), _p(ws), nbytes, _stream(dev))
     _lib.check(st)
+    if _lib.last_path() == 'tcgen05':
+        _check_device_error(ws, 'ccq_clean_bwd')
     return dq, dk, ((dW, db) if gate else dlam), dh0, dm0
 
 
@@ -163,8 +179,8 @@ class FusedCCQCleanRead(torch.autograd.Function):
         h0 = _state(initial_cov_state, (N, H, K, K))
         m0 = _state(initial_mean_state, (N, H, K)) if subtract_mean else None
         lam3 = reshape_lambda_3d(lambda_h, q)
-        qc, fcov, fmean, _ = clean_fwd_raw(q, k, lam3, None, None, position_offset, h0, m0, subtract_mean, cu, N)
-        ctx.save_for_backward(q, k, lam3, h0, m0, cu, fcov, fmean)
+        qc, fcov, fmean, aux = clean_fwd_raw(q, k, lam3, None, None, position_offset, h0, m0, subtract_mean, cu, N)
+        ctx.save_for_backward(q, k, lam3, h0, m0, cu, fcov, fmean, aux)
         ctx.lambda_h = lambda_h if isinstance(lambda_h, torch.Tensor) else None
         ctx.position_offset = int(position_offset)
         ctx.subtract_mean = bool(subtract_mean)
@@ -176,14 +192,14 @@ class FusedCCQCleanRead(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dqc, dfinal_cov, dfinal_mean):
-        q, k, lam3, h0, m0, cu, fcov, fmean = ctx.saved_tensors
+        q, k, lam3, h0, m0, cu, fcov, fmean, aux = ctx.saved_tensors
         lam_t = ctx.lambda_h
         need_dl = lam_t is not None and ctx.needs_input_grad[2]
         dqc = dqc.contiguous() if dqc.dtype == q.dtype else dqc.to(q.dtype).contiguous()
         dfc = dfinal_cov.float().contiguous() if dfinal_cov is not None else None
         dfm = dfinal_mean.float().contiguous() if dfinal_mean is not None else None
         dq, dk, dlam3, dh0, dm0 = clean_bwd_raw(q, k, lam3, None, None, ctx.position_offset, h0, m0,
-                                                ctx.subtract_mean, cu, ctx.N, fcov, fmean, dqc, dfc, dfm,
+                                                ctx.subtract_mean, cu, ctx.N, fcov, fmean, aux, dqc, dfc, dfm,
                                                 want_dlam=need_dl)
         dl = reduce_lambda_grad(dlam3, lam_t) if need_dl else None
         if dm0 is not None and not ctx.has_m0:
@@ -223,8 +239,8 @@ class FusedCCQCleanGated(torch.autograd.Function):
         cu, N = _seqs(B, cu_seqlens)
         h0 = _state(initial_cov_state, (N, H, K, K))
         m0 = _state(initial_mean_state, (N, H, K)) if subtract_mean else None
-        qc, fcov, fmean, _ = clean_fwd_raw(q, k, None, W, bb, position_offset, h0, m0, subtract_mean, cu, N)
-        ctx.save_for_backward(q, k, W, bb, h0, m0, cu, fcov, fmean)
+        qc, fcov, fmean, aux = clean_fwd_raw(q, k, None, W, bb, position_offset, h0, m0, subtract_mean, cu, N)
+        ctx.save_for_backward(q, k, W, bb, h0, m0, cu, fcov, fmean, aux)
         ctx.position_offset = int(position_offset)
         ctx.subtract_mean = bool(subtract_mean)
         ctx.N = N
@@ -236,12 +252,12 @@ class FusedCCQCleanGated(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dqc, dfinal_cov, dfinal_mean):
-        q, k, W, bb, h0, m0, cu, fcov, fmean = ctx.saved_tensors
+        q, k, W, bb, h0, m0, cu, fcov, fmean, aux = ctx.saved_tensors
         dqc = dqc.contiguous() if dqc.dtype == q.dtype else dqc.to(q.dtype).contiguous()
         dfc = dfinal_cov.float().contiguous() if dfinal_cov is not None else None
         dfm = dfinal_mean.float().contiguous() if dfinal_mean is not None else None
         dq, dk, (dW, db), dh0, dm0 = clean_bwd_raw(q, k, None, W, bb, ctx.position_offset, h0, m0,
-                                                   ctx.subtract_mean, cu, ctx.N, fcov, fmean, dqc, dfc, dfm)
+                                                   ctx.subtract_mean, cu, ctx.N, fcov, fmean, aux, dqc, dfc, dfm)
         if dm0 is not None and not ctx.has_m0:
             dm0 = None
         return dq, dk, dW.to(ctx.w_dtype), db.to(ctx.w_dtype), None, dh0, dm0, None, None, None

@@ -74,14 +74,15 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
  * Replaces FusedCCQCleanRead.forward / _fused_read_fwd (fused_read.py:379-403, :480-491).
  *   lambda_mode == CCQ_LAMBDA_TOKEN: lam [B,T,H] activation dtype; gate_w/gate_b unused.
  *   lambda_mode == CCQ_LAMBDA_GATE : gate_w [H,K] f32, gate_b [H] f32; lam unused.
- *   lam_out: optional [B,T,H] f32, receives the lambda used (GATE mode only).
+ *   token_aux: optional [B,T,H,2] f32 output, per token and head the lambda used and
+ *     s_t = m_t . q_t; the tensor-core backward reads it back instead of recomputing both.
  *   initial_cov / initial_mean: optional; initial_mean is ignored unless subtract_mean.
  *   final_cov / final_mean: optional outputs (the backward's tensor-core path reads them back).
  */
 int ccq_clean_fwd(int dtype, int B, int T, int H, int K,
                   const void* q, const void* k,
                   int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
-                  float* lam_out,
+                  float* token_aux,
                   const int64_t* cu_seqlens, int n_seqs,
                   int position_offset, int subtract_mean,
                   const float* initial_cov, const float* initial_mean,
@@ -91,9 +92,9 @@ int ccq_clean_fwd(int dtype, int B, int T, int H, int K,
 /*
  * Backward: dq, dk, dlambda (TOKEN mode) or dW/db (GATE mode), and the initial-state gradients.
  * Replaces FusedCCQCleanRead.backward / _fused_read_bwd (fused_read.py:406-460, :496-514).
- *   state_cov / state_mean: the final states the forward wrote for these inputs (required when
- *     the tensor-core path runs; pass NULL to let the library re-derive them, which costs an
- *     extra pass over k).
+ *   state_cov / state_mean / token_aux: the final states and per-token side outputs the forward
+ *     wrote for these inputs.  The tensor-core backward needs all three (it walks the chunks
+ *     backwards from the final state); when any is NULL the exact SIMT backward runs instead.
  *   dq_clean: upstream gradient [B,T,H,K]; dfinal_cov / dfinal_mean: optional state gradients.
  *   dlam: [B,T,H] f32 output (TOKEN mode), may be NULL when lambda needs no gradient.
  *   dgate_w [H,K] / dgate_b [H] f32 outputs (GATE mode; overwritten, summed over the batch).
@@ -106,7 +107,7 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K,
                   const int64_t* cu_seqlens, int n_seqs,
                   int position_offset, int subtract_mean,
                   const float* initial_cov, const float* initial_mean,
-                  const float* state_cov, const float* state_mean,
+                  const float* state_cov, const float* state_mean, const float* token_aux,
                   const void* dq_clean, const float* dfinal_cov, const float* dfinal_mean,
                   void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
                   float* dinitial_cov, float* dinitial_mean,

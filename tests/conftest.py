@@ -11,3 +11,7 @@ if HERE not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+# GPU tests synchronise after each tensor-core call and raise on a device pipeline timeout
+os.environ.setdefault('CCQ_B200_CHECK', '1')

@@ -165,8 +165,9 @@ def make_case(seed, B, T, H, K, lens=None, states=False, offset=0, final_grads=F
         d['h0'] = np.einsum('nthk,nthv->nhkv', kk, kk)
         d['m0'] = kk.sum(1)
     if final_grads:
-        d['dfc'] = rng.standard_normal((N, H, K, K))
-        d['dfm'] = rng.standard_normal((N, H, K)) if subtract_mean else None
+        # state gradients of realistic size: (dC + dC^T) k stays O(1) like the other gradient terms
+        d['dfc'] = rng.standard_normal((N, H, K, K)) / np.sqrt(K)
+        d['dfm'] = rng.standard_normal((N, H, K)) / np.sqrt(K) if subtract_mean else None
     return d, cu, offset, subtract_mean
 
 
@@ -327,3 +328,58 @@ def test_errors_raise():
         ccq_b200.fused_ccq_clean_read(q, q, 0.5, cu_seqlens=torch.tensor([0, 8], device='cuda'))
     with pytest.raises(RuntimeError):
         ccq_b200.fused_ccq_clean_read(q.cpu(), q.cpu(), 0.5)
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16], ids=['bf16', 'fp16'])
+@pytest.mark.parametrize('case', [
+    dict(B=2, T=1000, H=3, lens=None, states=True, off=0, gate=False, sm=True),
+    dict(B=1, T=0, H=2, lens=[300, 1, 128, 129, 7, 256], states=True, off=4, gate=False, sm=True),
+    dict(B=3, T=257, H=2, lens=None, states=False, off=-3, gate=True, sm=True),
+    dict(B=2, T=200, H=2, lens=None, states=True, off=0, gate=False, sm=False),
+], ids=['dense', 'varlen', 'gate', 'nomean'])
+def test_tcgen05_forward_path(case, dtype, monkeypatch):
+    """bf16/fp16 with K = 128 runs the tcgen05 forward; it agrees with the exact SIMT forward and the oracle."""
+    import ccq_b200
+    from ccq_b200 import ops
+    rng = np.random.default_rng(7)
+    lens = case['lens']
+    B, T, H, K = case['B'], case['T'], case['H'], 128
+    if lens is not None:
+        B, T = 1, int(sum(lens))
+    N = B if lens is None else len(lens)
+    cu = None if lens is None else dev(np.concatenate([[0], np.cumsum(lens)]), torch.int64)
+    q = dev(unit(rng, (B, T, H, K)), dtype)
+    k = dev(unit(rng, (B, T, H, K)), dtype)
+    lam = dev(rng.uniform(0, 1, (B, T, H)), dtype)
+    W = dev(rng.normal(0, 0.05, (H, K)))
+    b = dev(rng.uniform(-1, 1, H))
+    h0 = m0 = None
+    if case['states']:
+        kk = unit(rng, (N, 20, H, K))
+        h0 = dev(np.einsum('nthk,nthv->nhkv', kk, kk))
+        m0 = dev(kk.sum(1)) if case['sm'] else None
+    cu_, _ = ops._seqs(B, cu)
+
+    def run():
+        if case['gate']:
+            return ops.clean_fwd_raw(q, k, None, W, b, case['off'], h0, m0, case['sm'], cu_, N)
+        return ops.clean_fwd_raw(q, k, lam, None, None, case['off'], h0, m0, case['sm'], cu_, N)
+
+    qc, fc, fm, aux = run()
+    assert ccq_b200.last_path() == 'tcgen05'
+    monkeypatch.setenv('CCQ_B200_FORCE_SIMT', '1')
+    qs, fcs, fms, auxs = run()
+    assert ccq_b200.last_path() == 'simt'
+    monkeypatch.delenv('CCQ_B200_FORCE_SIMT')
+    assert (qc.float() - qs.float()).abs().max().item() <= BF16_TOL
+    assert rel_err(np64(fc), np64(fcs)) <= 1e-5
+    if case['sm']:
+        assert rel_err(np64(fm), np64(fms)) <= 1e-5
+    assert rel_err(np64(aux), np64(auxs)) <= 1e-3
+    # and the oracle on the rounded inputs
+    lam_np = (O.lambda_headwise_fwd(np64(q), np64(W), np64(b)) if case['gate'] else np64(lam))
+    oq, ofc, ofm = O.clean_read_fwd(np64(q), np64(k), lam_np, case['off'], None if h0 is None else np64(h0),
+                                    None if m0 is None else np64(m0), True, case['sm'],
+                                    None if cu is None else cu.cpu().numpy())
+    assert np.abs(np64(qc) - oq).max() <= BF16_TOL
+    assert rel_err(np64(fc), ofc) <= 1e-5
