@@ -1,4 +1,4 @@
-// Dispatch predicate of the tcgen05 path: bf16 / fp16 activations, K == 128, an sm_100 device.
+// Dispatch predicate of the tcgen05 paths: bf16 / fp16 activations, K == 128, an sm_100 device.
 #include <stdlib.h>
 #include <string.h>
 
@@ -29,15 +29,15 @@ bool tc_supported(const CleanArgs& a, int op) {
   if (a.dtype != DT_BF16 && a.dtype != DT_F16) return false;
   if (a.K != 128) return false;
   if ((int64_t)a.B * a.T >= (1ll << 31)) return false;
-  if (op == 1) return false;  // backward: not yet on tensor cores
   if (a.q && !(aligned16(a.q) && aligned16(a.k))) return false;
   if (a.q_clean && !aligned16(a.q_clean)) return false;
   if (a.initial_cov && !aligned16(a.initial_cov)) return false;
   if (a.final_cov && !aligned16(a.final_cov)) return false;
+  if (op == 1 && !(aligned16(a.dq_clean) && aligned16(a.dq) && aligned16(a.dk) &&
+                   aligned16(a.state_cov) && (a.dfinal_cov == nullptr || aligned16(a.dfinal_cov))))
+    return false;
   return device_major() == 10;
 }
 
-size_t tc_bwd_workspace(int, int, int, int, int) { return 0; }
-cudaError_t tc_bwd(const CleanArgs&, int*) { return cudaErrorNotSupported; }
 
 }  // namespace ccq

@@ -1,0 +1,706 @@
+// Tensor-core (tcgen05 / TMEM / TMA) backward of the CCQ cleaning operator, bf16 or fp16, K = 128.
+//
+// One CTA per (document, head) walks the document's chunks of BT = 64 tokens in REVERSE order.
+// The forward's final state (C_T, m_T) and its per-token side outputs (lambda_t, s_t) are inputs,
+// so the state before each chunk is recovered in TMEM (C -= K^T K, an MMA with negated A), and the
+// reverse-scan gradient G = dL/dC (after the chunk) is accumulated in TMEM as well; neither state
+// ever goes to HBM.  Per chunk, with Q, K, dQc = 64 x 128 tiles, alpha_t = lambda_t / pos_t:
+//   B1  [D ; A]  = [dQc ; Q] K^T                           (M = 128 stacked, N = 64)
+//   B5  C       -= K^T K                                   (-> C_prev)
+//   B2  [z ; dq] = [Q ; dZ] bf16(C_prev)                    dZ = -alpha dQc
+//   B2b [z ; dq] += [tril(A) ; P2] K                        P2 = (ds_t - alpha_t D)[j <= t]
+//   B3  dk^T     = Q^T P2 + dQc^T P4 + G K^T + G^T K^T      P4 = (beta_t - alpha_t A)[j <= t]
+//   B4  G       += Q^T dZ
+//   CW  [carry | dW] += Q^T [ds | dpre] + dQc^T [beta | 0]   (persistent 16-column accumulator)
+// with ds_t = lambda w_t / pos^2, beta_t = lambda s_t / pos^2, w_t = m_t . dqc_t, and
+//   dq_t = dqc_t + ds_t m_prev + [dq]_t (+ dpre_t W_h),  dlambda_t = -dqc_t . z_t / pos + s w / pos^2,
+//   dk_j = [dk^T]_j + carry  (the in-chunk dm suffix is folded into P2 and P4).
+// These are the reference's gradients (ccq/ops/common/fused_read.py:18-25, kernel :177-307,
+// carry :355-376, dC0 / dm0 :420-450).
+//
+// Warp roles (384 threads): warp 0 TMA, warp 1 TMEM + MMA issue, warps 2-3 aux (partial-chunk
+// key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.
+#include "args.h"
+#include "common.cuh"
+#include "tc_common.cuh"
+#include "tma_host.h"
+
+namespace ccq {
+
+namespace {
+using namespace tc;
+
+constexpr int B_THREADS = 384;
+constexpr int B_BT = 64;
+constexpr uint32_t B_QDPANEL = 24576;            // 192 rows: dQc (0-63), Q (64-127), dZ (128-191)
+constexpr uint32_t B_QDTILE = 2 * B_QDPANEL;
+constexpr uint32_t B_KPANEL = 8192;              // 64 rows
+constexpr uint32_t B_KTILE = 2 * B_KPANEL;
+constexpr uint32_t B_STAGE = B_QDTILE + B_KTILE; // 65536
+constexpr uint32_t B_OFF_K = B_QDTILE;           // inside a stage
+constexpr uint32_t B_OFF_C = 2 * B_STAGE;        // bf16 C_prev, 2 panels of 128 rows
+constexpr uint32_t B_OFF_G = B_OFF_C + 32768;    // bf16 G, 2 panels of 128 rows
+constexpr uint32_t B_OFF_AP = B_OFF_G + 32768;   // [tril(A) ; P2], 128 rows x 64
+constexpr uint32_t B_OFF_P4 = B_OFF_AP + 16384;  // P4, 64 rows x 64
+constexpr uint32_t B_OFF_R = B_OFF_P4 + 8192;    // R1, R2: 16 rows x 64 each (K-major, rows = columns)
+constexpr uint32_t B_OFF_SMALL = B_OFF_R + 4096; // 225280
+constexpr uint32_t T_C = 0, T_G = 128, T_ZQ = 256, T_DA = 384, T_CW = 448;
+
+struct BwdSmall {
+  float m_buf[2][128];
+  float wh[128];
+  float wpart[2][64], upart[2][64];
+  float w[64], ds[64], dpre[64];
+  uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
+  uint64_t tinit, da_full, c_full, cconv, cprev_free, pdone, gconv, g_full, zq_full, zq_free, dk_full, dk_read,
+      dpre_ready, cw_done, mma_done;
+  float db;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t B_SMEM = B_OFF_SMALL + sizeof(BwdSmall) + 1024;
+static_assert(B_SMEM <= 232448, "backward kernel shared memory");
+
+__device__ __forceinline__ void nbar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ bool nbar_any(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"((unsigned short)v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(taddr));
+  (void)r1; (void)r2; (void)r3;
+  return __uint_as_float(r0);
+}
+__device__ __forceinline__ void tmem_ld2f(uint32_t taddr, float* x) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(taddr));
+  (void)r2; (void)r3;
+  x[0] = __uint_as_float(r0);
+  x[1] = __uint_as_float(r1);
+}
+
+template <int AB16>
+__device__ __forceinline__ uint32_t to16(float x) {
+  if (AB16) return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+  return (uint32_t)__half_as_ushort(__float2half_rn(x));
+}
+
+// 8 consecutive 16-bit values of a swizzled panel row, as fp32
+template <int AB16>
+__device__ __forceinline__ void ld_row8(uint32_t panel, int row, int cc, float* f) {
+  const uint4 v = ld_shared_v4(panel + sw128(row, cc));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p = unpack2<AB16>(w[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+
+template <int AB16>
+__global__ void __launch_bounds__(B_THREADS, 1)
+    tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                  const __grid_constant__ CUtensorMap tmg, CleanArgs a, int* err, float* gate_part) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  BwdSmall& S = *reinterpret_cast<BwdSmall*>(sm + B_OFF_SMALL);
+  const uint32_t sbase = smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.H;
+  const int h = blockIdx.x % H, n = blockIdx.x / H;
+  const Seq sq = seq_of(n, a.T, a.cu_seqlens);
+  const int nchunks = (sq.len + B_BT - 1) / B_BT;
+  const int64_t st_base = ((int64_t)n * H + h) * 128;
+  const bool sub_mean = a.subtract_mean != 0;
+  const bool gate = a.lambda_mode == LAMBDA_GATE;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.kready[i], 1);
+      mbar_init(&S.empty[i], 3);
+      mbar_init(&S.m_ready[i], 1);
+      mbar_init(&S.m_free[i], 1);
+    }
+    uint64_t* singles[] = {&S.tinit, &S.da_full, &S.c_full, &S.cconv, &S.cprev_free, &S.pdone, &S.gconv, &S.g_full,
+                           &S.zq_full, &S.zq_free, &S.dk_full, &S.dk_read, &S.dpre_ready, &S.cw_done, &S.mma_done};
+    for (uint64_t* b : singles) mbar_init(b, 1);
+    S.abort = 0;
+    S.db = 0.f;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&S.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (chunks in reverse)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmg);
+      int issued = 0;
+      for (int i = 0; i < nchunks; ++i) {
+        const int s = i & 1, c = nchunks - 1 - i;
+        if (i >= 2 && !mbar_wait(&S.empty[s], ((i - 2) >> 1) & 1)) {
+          atomicOr(err, 1);
+          S.abort = 1;
+          break;
+        }
+        if (*(volatile int*)&S.abort) break;
+        mbar_arrive_expect_tx(&S.full[s], 6 * 8192);
+        const int row = (int)(sq.bos + (int64_t)c * B_BT);
+        uint8_t* st = sm + s * B_STAGE;
+        tma_load_3d(st, &tmg, &S.full[s], 0, h, row);
+        tma_load_3d(st + B_QDPANEL, &tmg, &S.full[s], 64, h, row);
+        tma_load_3d(st + 8192, &tmq, &S.full[s], 0, h, row);
+        tma_load_3d(st + B_QDPANEL + 8192, &tmq, &S.full[s], 64, h, row);
+        tma_load_3d(st + B_OFF_K, &tmk, &S.full[s], 0, h, row);
+        tma_load_3d(st + B_OFF_K + B_KPANEL, &tmk, &S.full[s], 64, h, row);
+        ++issued;
+      }
+      for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i) mbar_wait(&S.full[i & 1], (i >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_b1 = idesc_f16(128, 64, AB16, 0, 0);
+      const uint32_t id_b5 = idesc_f16(128, 128, AB16, 1, 1, 1);
+      const uint32_t id_b2 = idesc_f16(128, 128, AB16, 0, 1);
+      const uint32_t id_b3mm = idesc_f16(128, 64, AB16, 1, 1);
+      const uint32_t id_b3kk = idesc_f16(128, 64, AB16, 0, 0);
+      const uint32_t id_b3mk = idesc_f16(128, 64, AB16, 1, 0);
+      const uint32_t id_b4 = idesc_f16(128, 128, AB16, 1, 1);
+      const uint32_t id_cw = idesc_f16(128, 16, AB16, 1, 0);
+      const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
+                     sR = sbase + B_OFF_R;
+      bool ok = mbar_wait(&S.tinit, 0);
+      auto cw = [&](int i) {  // carry / dW accumulation of iteration i
+        const uint32_t st = sbase + (i & 1) * B_STAGE;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_CW, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024), sdesc(sR + ks * 32, 16, 1024), id_cw, 1);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_CW, sdesc(st + ks * 2048, B_QDPANEL, 1024), sdesc(sR + 2048 + ks * 32, 16, 1024), id_cw, 1);
+        umma_commit(&S.cw_done);
+        umma_commit(&S.empty[i & 1]);
+      };
+      for (int i = 0; i < nchunks && ok; ++i) {
+        const int s = i & 1;
+        const uint32_t st = sbase + s * B_STAGE, sK = st + B_OFF_K;
+        ok = mbar_wait(&S.kready[s], (i >> 1) & 1) && (i == 0 || mbar_wait(&S.dk_read, (i - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        // B1: [D ; A] = [dQc ; Q] K^T
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_DA, sdesc(st + (ks >> 2) * B_QDPANEL + (ks & 3) * 32, 16, 1024),
+               sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b1, ks > 0);
+        umma_commit(&S.da_full);
+        if (i >= 1) {
+          ok = mbar_wait(&S.dpre_ready, (i - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          cw(i - 1);
+          ok = mbar_wait(&S.cconv, (i - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        // B5: C -= K^T K  (C_prev of this chunk)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_C, sdesc(sK + ks * 2048, B_KPANEL, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b5, 1);
+        umma_commit(&S.c_full);
+        ok = mbar_wait(&S.pdone, i & 1) && mbar_wait(&S.cconv, i & 1) && mbar_wait(&S.gconv, i & 1) &&
+             (i == 0 || mbar_wait(&S.zq_free, (i - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        // B2 / B2b: [z ; dq] = [Q ; dZ] C_prev + [tril(A) ; P2] K
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_ZQ, sdesc(st + (ks >> 2) * B_QDPANEL + 8192 + (ks & 3) * 32, 16, 1024),
+               sdesc(sC + ks * 2048, 16384, 1024), id_b2, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_ZQ, sdesc(sAP + ks * 32, 16, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b2, 1);
+        umma_commit(&S.zq_full);
+        umma_commit(&S.cprev_free);
+        // B4: G += Q^T dZ
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_G, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024),
+               sdesc(st + 16384 + ks * 2048, B_QDPANEL, 1024), id_b4, 1);
+        umma_commit(&S.g_full);
+        // B3: dk^T = Q^T P2 + dQc^T P4 + G K^T + G^T K^T   (columns shared with [D ; A])
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_DA, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024), sdesc(sAP + 8192 + ks * 2048, 8192, 1024),
+               id_b3mm, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_DA, sdesc(st + ks * 2048, B_QDPANEL, 1024), sdesc(sP4 + ks * 2048, 8192, 1024), id_b3mm, 1);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_DA, sdesc(sG + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+               sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b3kk, 1);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma(tbase + T_DA, sdesc(sG + ks * 2048, 16384, 1024),
+               sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b3mk, 1);
+        umma_commit(&S.dk_full);
+      }
+      if (ok && nchunks > 0) {
+        ok = mbar_wait(&S.dk_read, (nchunks - 1) & 1) && mbar_wait(&S.dpre_ready, (nchunks - 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          cw(nchunks - 1);
+        }
+      }
+      if (!ok) {
+        atomicOr(err, 2);
+        S.abort = 1;
+      }
+      umma_commit(&S.mma_done);
+      mbar_wait(&S.mma_done, 0);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ aux: zero ragged keys, walk m backwards
+    const int at = threadIdx.x - 64;
+    const uint32_t p = at >> 5;
+    const uint32_t e = (2 * at) & 63;
+    const uint32_t ch = e >> 3, cb = (e & 7) * 2;
+    float m0v = 0.f, m1v = 0.f;
+    if (sub_mean && a.state_mean) {
+      m0v = a.state_mean[st_base + 2 * at];
+      m1v = a.state_mean[st_base + 2 * at + 1];
+    }
+    for (int i = 0; i < nchunks; ++i) {
+      const int s = i & 1, c = nchunks - 1 - i;
+      const bool ok = mbar_wait(&S.full[s], (i >> 1) & 1);
+      if (nbar_any(2, 64, !ok)) {
+        if (at == 0) { atomicOr(err, 4); S.abort = 1; }
+        break;
+      }
+      const uint32_t kt = sbase + s * B_STAGE + B_OFF_K;
+      const int valid = min(B_BT, sq.len - c * B_BT);
+      if (valid < B_BT) {
+        const uint32_t wp = at >> 5, wi = at & 31;
+        for (int rr = valid; rr < B_BT; ++rr) st_shared_u32(kt + wp * B_KPANEL + sw128(rr, wi >> 2) + (wi & 3) * 4, 0u);
+        fence_async_smem();
+      }
+      nbar_sync(2, 64);
+      if (at == 0) mbar_arrive(&S.kready[s]);
+      if (sub_mean) {
+        float acc0 = 0.f, acc1 = 0.f;
+        const uint32_t kb = kt + p * B_KPANEL + cb;
+#pragma unroll 8
+        for (int tt = 0; tt < B_BT; ++tt) {
+          const float2 f = unpack2<AB16>(ld_shared_u32(kb + sw128(tt, ch)));
+          acc0 += f.x;
+          acc1 += f.y;
+        }
+        m0v -= acc0;
+        m1v -= acc1;
+      }
+      const bool ok2 = (i < 2) || mbar_wait(&S.m_free[s], ((i - 2) >> 1) & 1);
+      if (nbar_any(2, 64, !ok2)) {
+        if (at == 0) { atomicOr(err, 8); S.abort = 1; }
+        break;
+      }
+      S.m_buf[s][2 * at] = m0v;
+      S.m_buf[s][2 * at + 1] = m1v;
+      nbar_sync(2, 64);
+      if (at == 0) {
+        mbar_arrive(&S.m_ready[s]);
+        mbar_arrive(&S.empty[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (256 threads)
+    const int et = threadIdx.x - 128;
+    const int g = et >> 7;
+    const int qd = warp & 3;
+    const int r = 32 * qd + lane;
+    const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
+    const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
+                   sR = sbase + B_OFF_R;
+    float v[64];
+    // initial TMEM: C = C_T, G = dC_T, [carry | dW] = [dm_T | 0]
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int col0 = 64 * g + 32 * hf;
+      const float4* src = reinterpret_cast<const float4*>(a.state_cov + (st_base + r) * 128 + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 f = src[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+      }
+      tmem_st32(lrow + T_C + col0, v);
+      if (a.dfinal_cov) {
+        const float4* d4 = reinterpret_cast<const float4*>(a.dfinal_cov + (st_base + r) * 128 + col0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 f = d4[i];
+          v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      tmem_st32(lrow + T_G + col0, v);
+    }
+    if (g == 0) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      if (a.dfinal_mean) v[0] = a.dfinal_mean[st_base + r];
+      tmem_st32(lrow + T_CW, v);
+    }
+    if (gate && et < 128) S.wh[et] = a.gate_w[(int64_t)h * 128 + et];
+    st_shared_v4(sR + 16 * et, 0u, 0u, 0u, 0u);  // R1, R2: columns that stay zero
+    fence_async_smem();
+    tmem_st_wait();
+    tc_fence_before();
+    nbar_sync(1, 256);
+    if (et == 0) mbar_arrive(&S.tinit);
+    float db_acc = 0.f;
+
+    for (int i = 0; i < nchunks; ++i) {
+      const int s = i & 1, c = nchunks - 1 - i;
+      const int t0 = c * B_BT;
+      const int valid = min(B_BT, sq.len - t0);
+      const uint32_t st = sbase + s * B_STAGE;
+      bool ok;
+      // ---------------- G (after this chunk) -> bf16 operand
+      ok = (i == 0) || mbar_wait(&S.g_full, (i - 1) & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 16); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_G + 64 * g, v);
+      tmem_ld32(lrow + T_G + 64 * g + 32, v + 32);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        st_shared_v4(sG + g * 16384 + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
+                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
+                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+      fence_async_smem();
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.gconv);
+
+      // ---------------- E1: P2, tril(A), P4, dZ, R columns
+      ok = mbar_wait(&S.da_full, i & 1) && mbar_wait(&S.m_ready[s], (i >> 1) & 1) &&
+           (i == 0 || mbar_wait(&S.cw_done, (i - 1) & 1));
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 32); S.abort = 1; } break; }
+      tc_fence_after();
+      const bool dside = r < 64;
+      const int t = dside ? r : r - 64;
+      const bool tv = t < valid;
+      float lamv = 0.f, sv = 0.f;
+      if (tv) {
+        const float2 ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
+        lamv = ax.x;
+        sv = sub_mean ? ax.y : 0.f;
+      }
+      const float ipos = 1.f / position_of(t0 + t, a.position_offset);
+      const float alpha = lamv * ipos;
+      tmem_ld32(lrow + T_DA + 32 * g, v);
+      const float* mp = S.m_buf[s];
+      if (dside) {
+        // w partial: sum_{j <= t} D[t][j] over my 32 columns + m_prev . dqc_t over my 64 dims
+        float wp = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) wp += (32 * g + jj <= t) ? v[jj] : 0.f;
+        if (sub_mean) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            float f[8];
+            ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
+#pragma unroll
+            for (int e2 = 0; e2 < 8; ++e2) wp = fmaf(mp[64 * g + 8 * cc + e2], f[e2], wp);
+          }
+        }
+        S.wpart[g][t] = wp;
+      } else {
+        // tril(A) rows and P4 need only this thread's data; dZ = -alpha dqc for my 64 dims
+        const float beta = sub_mean ? lamv * sv * ipos * ipos : 0.f;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t am[4], p4[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int jj = 8 * q4 + 2 * e2, j = 32 * g + jj;
+            const float a0 = j <= t ? v[jj] : 0.f, a1 = j + 1 <= t ? v[jj + 1] : 0.f;
+            am[e2] = pack2<AB16>(a0, a1);
+            const float p0 = (j <= t && tv) ? beta - alpha * v[jj] : 0.f;
+            const float p1 = (j + 1 <= t && tv) ? beta - alpha * v[jj + 1] : 0.f;
+            p4[e2] = pack2<AB16>(p0, p1);
+          }
+          st_shared_v4(sAP + sw128(t, 4 * g + q4), am[0], am[1], am[2], am[3]);
+          st_shared_v4(sP4 + sw128(t, 4 * g + q4), p4[0], p4[1], p4[2], p4[3]);
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float f[8];
+          ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
+          st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), pack2<AB16>(-alpha * f[0], -alpha * f[1]),
+                       pack2<AB16>(-alpha * f[2], -alpha * f[3]), pack2<AB16>(-alpha * f[4], -alpha * f[5]),
+                       pack2<AB16>(-alpha * f[6], -alpha * f[7]));
+        }
+        if (g == 0) st_shared_u16(sR + 2048 + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(tv ? beta : 0.f));
+      }
+      nbar_sync(1, 256);
+      if (dside) {
+        const float w = S.wpart[0][t] + S.wpart[1][t];
+        const float ds = sub_mean ? lamv * w * ipos * ipos : 0.f;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t p2[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int jj = 8 * q4 + 2 * e2, j = 32 * g + jj;
+            const float p0 = (j <= t && tv) ? ds - alpha * v[jj] : 0.f;
+            const float p1 = (j + 1 <= t && tv) ? ds - alpha * v[jj + 1] : 0.f;
+            p2[e2] = pack2<AB16>(p0, p1);
+          }
+          st_shared_v4(sAP + 8192 + sw128(t, 4 * g + q4), p2[0], p2[1], p2[2], p2[3]);
+        }
+        if (g == 0) {
+          S.w[t] = w;
+          S.ds[t] = tv ? ds : 0.f;
+          st_shared_u16(sR + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(tv ? ds : 0.f));
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.pdone);
+
+      // ---------------- C_prev -> bf16 operand
+      ok = mbar_wait(&S.c_full, i & 1) && (i == 0 || mbar_wait(&S.cprev_free, (i - 1) & 1));
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 64); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_C + 64 * g, v);
+      tmem_ld32(lrow + T_C + 64 * g + 32, v + 32);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        st_shared_v4(sC + g * 16384 + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
+                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
+                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+      fence_async_smem();
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.cconv);
+
+      // ---------------- E2: dlambda (z side) and dq (dq side)
+      ok = mbar_wait(&S.zq_full, i & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 128); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_ZQ + 64 * g, v);
+      tmem_ld32(lrow + T_ZQ + 64 * g + 32, v + 32);
+      if (dside) {  // lanes 0-63 hold z
+        float up = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float f[8];
+          ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
+#pragma unroll
+          for (int e2 = 0; e2 < 8; ++e2) up = fmaf(f[e2], v[8 * cc + e2], up);
+        }
+        S.upart[g][t] = up;
+      }
+      nbar_sync(1, 256);
+      if (dside && g == 0) {
+        const float u = S.upart[0][t] + S.upart[1][t];
+        float dl = -u * ipos;
+        if (sub_mean) dl += sv * S.w[t] * ipos * ipos;
+        const int64_t tok = (sq.bos + t0 + t) * H + h;
+        float dp = 0.f;
+        if (gate) dp = tv ? dl * lamv * (1.f - lamv) : 0.f;
+        else if (tv && a.dlam) a.dlam[tok] = dl;
+        S.dpre[t] = dp;
+        st_shared_u16(sR + sw128(1, t >> 3) + (t & 7) * 2, to16<AB16>(dp));
+        db_acc += dp;
+      }
+      if (gate) nbar_sync(1, 256);
+      if (!dside) {  // lanes 64-127 hold the dq accumulator
+        const float ds = S.ds[t];
+        const float dp = gate ? S.dpre[t] : 0.f;
+        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float f[8];
+          ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
+          uint32_t o[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int d0 = 64 * g + 8 * cc + 2 * e2;
+            float x0 = f[2 * e2] + ds * mp[d0] + v[8 * cc + 2 * e2];
+            float x1 = f[2 * e2 + 1] + ds * mp[d0 + 1] + v[8 * cc + 2 * e2 + 1];
+            if (gate) {
+              x0 = fmaf(dp, S.wh[d0], x0);
+              x1 = fmaf(dp, S.wh[d0 + 1], x1);
+            }
+            o[e2] = pack2<AB16>(x0, x1);
+          }
+          if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) {
+        mbar_arrive(&S.zq_free);
+        mbar_arrive(&S.dpre_ready);
+        mbar_arrive(&S.m_free[s]);
+      }
+
+      // ---------------- E3: dk = dk^T + carry, staged through the K tile
+      ok = mbar_wait(&S.dk_full, i & 1);
+      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 256); S.abort = 1; } break; }
+      tc_fence_after();
+      tmem_ld32(lrow + T_DA + 32 * g, v);
+      const float carry = tmem_ld1(lrow + T_CW);
+      {
+        const uint32_t kpanel = st + B_OFF_K + (r >> 6) * B_KPANEL + ((r & 7) * 2);
+        const uint32_t rc = (r & 63) >> 3;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + carry));
+      }
+      tc_fence_before();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.dk_read);
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int qid = et + 256 * k4;             // 16-byte chunk id: row (64) x panel (2) x chunk (8)
+        const int row = qid >> 4, pn = (qid >> 3) & 1, cc = qid & 7;
+        if (row < valid) {
+          const uint4 val = ld_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, cc));
+          *reinterpret_cast<uint4*>((uint8_t*)a.dk + (((sq.bos + t0 + row) * H + h) * 128 + 64 * pn + 8 * cc) * 2) = val;
+        }
+      }
+      fence_async_smem();
+      nbar_sync(1, 256);
+      if (et == 0) mbar_arrive(&S.empty[s]);
+    }
+    // ---------------- per-document outputs
+    if (!nbar_any(1, 256, *(volatile int*)&S.abort != 0)) {
+      const bool okf = (nchunks == 0) || (mbar_wait(&S.g_full, (nchunks - 1) & 1) &&
+                                          mbar_wait(&S.cw_done, (nchunks - 1) & 1));
+      if (!nbar_any(1, 256, !okf)) {
+        tc_fence_after();
+        if (a.dinitial_cov) {
+          tmem_ld32(lrow + T_G + 64 * g, v);
+          tmem_ld32(lrow + T_G + 64 * g + 32, v + 32);
+          float4* dst = reinterpret_cast<float4*>(a.dinitial_cov + (st_base + r) * 128 + 64 * g);
+#pragma unroll
+          for (int k4 = 0; k4 < 16; ++k4) dst[k4] = make_float4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]);
+        }
+        float cwv[2];
+        tmem_ld2f(lrow + T_CW, cwv);
+        if (g == 0 && a.dinitial_mean) a.dinitial_mean[st_base + r] = cwv[0];
+        if (g == 0 && gate) gate_part[((int64_t)n * H + h) * 129 + r] = cwv[1];
+      } else if (et == 0) {
+        atomicOr(err, 512);
+      }
+    }
+    if (gate) {
+      db_acc = warp_sum(db_acc);
+      if (lane == 0 && db_acc != 0.f) atomicAdd(&S.db, db_acc);
+      nbar_sync(1, 256);
+      if (et == 0) gate_part[((int64_t)n * H + h) * 129 + 128] = S.db;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// dW[h] = sum over documents of the per-CTA partials, db[h] likewise
+__global__ void gate_sum_kernel(const float* part, int n_seqs, int H, float* dW, float* db) {
+  const int h = blockIdx.x;
+  for (int d = threadIdx.x; d <= 128; d += blockDim.x) {
+    float s = 0.f;
+    for (int n = 0; n < n_seqs; ++n) s += part[((int64_t)n * H + h) * 129 + d];
+    if (d < 128) dW[(int64_t)h * 128 + d] = s;
+    else db[h] = s;
+  }
+}
+
+template <int AB16>
+cudaError_t launch(const CleanArgs& a, int* launches) {
+  CUtensorMap tq, tk, tg;
+  const int64_t rows = (int64_t)a.B * a.T;
+  cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, B_BT, AB16 != 0);
+  if (e != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&tg, a.dq_clean, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
+  int* err = reinterpret_cast<int*>(a.workspace);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
+  if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
+  auto kern = tc_bwd_kernel<AB16>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
+    return e;
+  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, a, err, part);
+  *launches += 1;
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (a.lambda_mode == LAMBDA_GATE) {
+    gate_sum_kernel<<<a.H, 128, 0, a.stream>>>(part, a.n_seqs, a.H, a.dgate_w, a.dgate_b);
+    *launches += 1;
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+size_t tc_bwd_workspace(int, int, int H, int, int n_seqs) {
+  return 256 + ws_align(sizeof(float) * (size_t)n_seqs * H * 129);
+}
+
+cudaError_t tc_bwd(const CleanArgs& a, int* launches) {
+  return a.dtype == DT_BF16 ? launch<1>(a, launches) : launch<0>(a, launches);
+}
+
+}  // namespace ccq

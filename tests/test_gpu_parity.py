@@ -383,3 +383,75 @@ def test_tcgen05_forward_path(case, dtype, monkeypatch):
                                     None if cu is None else cu.cpu().numpy())
     assert np.abs(np64(qc) - oq).max() <= BF16_TOL
     assert rel_err(np64(fc), ofc) <= 1e-5
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float16], ids=['bf16', 'fp16'])
+@pytest.mark.parametrize('case', [
+    dict(B=2, T=1000, H=3, lens=None, states=True, off=0, gate=False, sm=True, fg=True),
+    dict(B=1, T=0, H=2, lens=[300, 1, 64, 65, 7, 256], states=True, off=4, gate=False, sm=True, fg=True),
+    dict(B=3, T=257, H=2, lens=None, states=False, off=-3, gate=True, sm=True, fg=False),
+    dict(B=2, T=200, H=2, lens=None, states=True, off=0, gate=False, sm=False, fg=True),
+    dict(B=1, T=63, H=4, lens=None, states=False, off=0, gate=True, sm=True, fg=False),
+], ids=['dense', 'varlen', 'gate', 'nomean', 'short'])
+def test_tcgen05_backward_path(case, dtype, monkeypatch):
+    """bf16/fp16 with K = 128 runs the tcgen05 backward; it agrees with the exact SIMT backward and the oracle."""
+    import ccq_b200
+    from ccq_b200 import ops
+    rng = np.random.default_rng(11)
+    lens = case['lens']
+    B, T, H, K = case['B'], case['T'], case['H'], 128
+    if lens is not None:
+        B, T = 1, int(sum(lens))
+    N = B if lens is None else len(lens)
+    cu = None if lens is None else dev(np.concatenate([[0], np.cumsum(lens)]), torch.int64)
+    q = dev(unit(rng, (B, T, H, K)), dtype)
+    k = dev(unit(rng, (B, T, H, K)), dtype)
+    lam = dev(rng.uniform(0, 1, (B, T, H)), dtype)
+    g = dev(rng.standard_normal((B, T, H, K)), dtype)
+    W = dev(rng.normal(0, 0.05, (H, K)))
+    b = dev(rng.uniform(-1, 1, H))
+    h0 = m0 = dfc = dfm = None
+    if case['states']:
+        kk = unit(rng, (N, 20, H, K))
+        h0 = dev(np.einsum('nthk,nthv->nhkv', kk, kk))
+        m0 = dev(kk.sum(1)) if case['sm'] else None
+    if case['fg']:
+        dfc = dev(rng.standard_normal((N, H, K, K)) / np.sqrt(K))
+        dfm = dev(rng.standard_normal((N, H, K)) / np.sqrt(K)) if case['sm'] else None
+    cu_, _ = ops._seqs(B, cu)
+    gw, gb = (W, b) if case['gate'] else (None, None)
+    lam3 = None if case['gate'] else lam
+
+    qc, fc, fm, aux = ops.clean_fwd_raw(q, k, lam3, gw, gb, case['off'], h0, m0, case['sm'], cu_, N)
+    res = ops.clean_bwd_raw(q, k, lam3, gw, gb, case['off'], h0, m0, case['sm'], cu_, N, fc, fm, aux, g, dfc, dfm)
+    assert ccq_b200.last_path() == 'tcgen05'
+    monkeypatch.setenv('CCQ_B200_FORCE_SIMT', '1')
+    ref = ops.clean_bwd_raw(q, k, lam3, gw, gb, case['off'], h0, m0, case['sm'], cu_, N, fc, fm, aux, g, dfc, dfm)
+    assert ccq_b200.last_path() == 'simt'
+    monkeypatch.delenv('CCQ_B200_FORCE_SIMT')
+    dq, dk, dl, dh0, dm0 = res
+    rdq, rdk, rdl, rdh0, rdm0 = ref
+    assert (dq.float() - rdq.float()).abs().max().item() <= BF16_TOL
+    assert (dk.float() - rdk.float()).abs().max().item() <= BF16_TOL
+    if case['gate']:
+        assert rel_err(np64(dl[0]), np64(rdl[0])) <= 1e-2
+        assert rel_err(np64(dl[1]), np64(rdl[1])) <= 1e-2
+    else:
+        assert (dl - rdl).abs().max().item() <= BF16_TOL
+    if h0 is not None:
+        assert rel_err(np64(dh0), np64(rdh0)) <= 1e-2
+    if dm0 is not None:
+        assert rel_err(np64(dm0), np64(rdm0)) <= 1e-2
+    # oracle on the rounded inputs
+    qn, kn, gn = np64(q), np64(k), np64(g)
+    lam_np = O.lambda_headwise_fwd(qn, np64(W), np64(b)) if case['gate'] else np64(lam)
+    cun = None if cu is None else cu.cpu().numpy()
+    odq, odk, odl, _, _ = O.clean_read_bwd(qn, kn, lam_np, gn, case['off'], None if h0 is None else np64(h0),
+                                           None if m0 is None else np64(m0), case['sm'], cun,
+                                           None if dfc is None else np64(dfc), None if dfm is None else np64(dfm))
+    if case['gate']:
+        dqx, oW, ob = O.lambda_headwise_bwd(qn, np64(W), lam_np, odl)
+        odq = odq + dqx
+        assert rel_err(np64(dl[0]), oW) <= 1e-2
+    assert np.abs(np64(dq) - odq).max() <= BF16_TOL
+    assert np.abs(np64(dk) - odk).max() <= BF16_TOL
