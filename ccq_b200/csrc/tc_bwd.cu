@@ -52,28 +52,17 @@ struct BwdSmall {
   float wpart[2][64], upart[2][64];
   float w[64], ds[64], dpre[64];
   uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
-  uint64_t tinit, da_full, c_full, cconv, cprev_free, pdone, gconv, g_full, zq_full, zq_free, dk_full, dk_read,
-      dpre_ready, cw_done, mma_done;
+  uint64_t tinit, da_full, c_full, c_read, cconv, cprev_free, pdone, gconv, g_full, zq_full, zq_free, dk_full,
+      dk_read, dpre_ready, cw_done, mma_done;
   float db;
   uint32_t tmem_base;
   int abort;
 };
 constexpr size_t B_SMEM = B_OFF_SMALL + sizeof(BwdSmall) + 1024;
 static_assert(B_SMEM <= 232448, "backward kernel shared memory");
+constexpr int EPI_WARPS = 8;
 
 __device__ __forceinline__ void nbar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ bool nbar_any(int id, int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -93,16 +82,7 @@ __device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
   asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
-__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
-  uint32_t r0, r1, r2, r3;
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(taddr));
-  (void)r1; (void)r2; (void)r3;
-  return __uint_as_float(r0);
-}
+// the first two of 4 consecutive fp32 TMEM columns of this thread's lane
 __device__ __forceinline__ void tmem_ld2f(uint32_t taddr, float* x) {
   uint32_t r0, r1, r2, r3;
   asm volatile(
@@ -110,9 +90,10 @@ __device__ __forceinline__ void tmem_ld2f(uint32_t taddr, float* x) {
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
       : "r"(taddr));
-  (void)r2; (void)r3;
   x[0] = __uint_as_float(r0);
   x[1] = __uint_as_float(r1);
+  (void)r2;
+  (void)r3;
 }
 
 template <int AB16>
@@ -132,6 +113,14 @@ __device__ __forceinline__ void ld_row8(uint32_t panel, int row, int cc, float* 
     f[2 * i] = p.x;
     f[2 * i + 1] = p.y;
   }
+}
+
+template <int AB16>
+__device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const float* v) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+    st_shared_v4(panel + sw128(row, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]), pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]),
+                 pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]), pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
 }
 
 template <int AB16>
@@ -155,13 +144,15 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.kready[i], 1);
-      mbar_init(&S.empty[i], 3);
+      mbar_init(&S.empty[i], 2 + EPI_WARPS);
       mbar_init(&S.m_ready[i], 1);
-      mbar_init(&S.m_free[i], 1);
+      mbar_init(&S.m_free[i], EPI_WARPS);
     }
-    uint64_t* singles[] = {&S.tinit, &S.da_full, &S.c_full, &S.cconv, &S.cprev_free, &S.pdone, &S.gconv, &S.g_full,
-                           &S.zq_full, &S.zq_free, &S.dk_full, &S.dk_read, &S.dpre_ready, &S.cw_done, &S.mma_done};
-    for (uint64_t* b : singles) mbar_init(b, 1);
+    uint64_t* ones[] = {&S.da_full, &S.c_full, &S.cprev_free, &S.g_full, &S.zq_full, &S.dk_full, &S.cw_done,
+                        &S.mma_done};
+    for (uint64_t* b : ones) mbar_init(b, 1);
+    uint64_t* epis[] = {&S.tinit, &S.c_read, &S.cconv, &S.pdone, &S.gconv, &S.zq_free, &S.dk_read, &S.dpre_ready};
+    for (uint64_t* b : epis) mbar_init(b, EPI_WARPS);
     S.abort = 0;
     S.db = 0.f;
     fence_barrier_init();
@@ -171,6 +162,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = S.tmem_base;
+  volatile int* ab = &S.abort;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (chunks in reverse)
@@ -181,12 +173,8 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
         const int s = i & 1, c = nchunks - 1 - i;
-        if (i >= 2 && !mbar_wait(&S.empty[s], ((i - 2) >> 1) & 1)) {
-          atomicOr(err, 1);
-          S.abort = 1;
-          break;
-        }
-        if (*(volatile int*)&S.abort) break;
+        if (i >= 2 && !pipe_wait(&S.empty[s], ((i - 2) >> 1) & 1, ab, err, 1)) break;
+        if (*ab) break;
         mbar_arrive_expect_tx(&S.full[s], 6 * 8192);
         const int row = (int)(sq.bos + (int64_t)c * B_BT);
         uint8_t* st = sm + s * B_STAGE;
@@ -213,7 +201,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const uint32_t id_cw = idesc_f16(128, 16, AB16, 1, 0);
       const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
                      sR = sbase + B_OFF_R;
-      bool ok = mbar_wait(&S.tinit, 0);
       auto cw = [&](int i) {  // carry / dW accumulation of iteration i
         const uint32_t st = sbase + (i & 1) * B_STAGE;
 #pragma unroll
@@ -225,10 +212,12 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         umma_commit(&S.cw_done);
         umma_commit(&S.empty[i & 1]);
       };
+      bool ok = pipe_wait(&S.tinit, 0, ab, err, 2);
       for (int i = 0; i < nchunks && ok; ++i) {
         const int s = i & 1;
         const uint32_t st = sbase + s * B_STAGE, sK = st + B_OFF_K;
-        ok = mbar_wait(&S.kready[s], (i >> 1) & 1) && (i == 0 || mbar_wait(&S.dk_read, (i - 1) & 1));
+        ok = pipe_wait(&S.kready[s], (i >> 1) & 1, ab, err, 2) &&
+             (i == 0 || pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2));
         if (!ok) break;
         tc_fence_after();
         // B1: [D ; A] = [dQc ; Q] K^T
@@ -238,11 +227,11 @@ __global__ void __launch_bounds__(B_THREADS, 1)
                sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b1, ks > 0);
         umma_commit(&S.da_full);
         if (i >= 1) {
-          ok = mbar_wait(&S.dpre_ready, (i - 1) & 1);
+          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
           tc_fence_after();
           cw(i - 1);
-          ok = mbar_wait(&S.cconv, (i - 1) & 1);
+          ok = pipe_wait(&S.c_read, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
           tc_fence_after();
         }
@@ -251,8 +240,8 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         for (int ks = 0; ks < 4; ++ks)
           umma(tbase + T_C, sdesc(sK + ks * 2048, B_KPANEL, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b5, 1);
         umma_commit(&S.c_full);
-        ok = mbar_wait(&S.pdone, i & 1) && mbar_wait(&S.cconv, i & 1) && mbar_wait(&S.gconv, i & 1) &&
-             (i == 0 || mbar_wait(&S.zq_free, (i - 1) & 1));
+        ok = pipe_wait(&S.pdone, i & 1, ab, err, 2) && pipe_wait(&S.cconv, i & 1, ab, err, 2) &&
+             pipe_wait(&S.gconv, i & 1, ab, err, 2) && (i == 0 || pipe_wait(&S.zq_free, (i - 1) & 1, ab, err, 2));
         if (!ok) break;
         tc_fence_after();
         // B2 / B2b: [z ; dq] = [Q ; dZ] C_prev + [tril(A) ; P2] K
@@ -265,12 +254,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           umma(tbase + T_ZQ, sdesc(sAP + ks * 32, 16, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b2, 1);
         umma_commit(&S.zq_full);
         umma_commit(&S.cprev_free);
-        // B4: G += Q^T dZ
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma(tbase + T_G, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024),
-               sdesc(st + 16384 + ks * 2048, B_QDPANEL, 1024), id_b4, 1);
-        umma_commit(&S.g_full);
         // B3: dk^T = Q^T P2 + dQc^T P4 + G K^T + G^T K^T   (columns shared with [D ; A])
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
@@ -288,17 +271,20 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           umma(tbase + T_DA, sdesc(sG + ks * 2048, 16384, 1024),
                sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b3mk, 1);
         umma_commit(&S.dk_full);
+        // B4: G += Q^T dZ  (the bf16 copy B3 just read was taken before)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma(tbase + T_G, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024),
+               sdesc(st + 16384 + ks * 2048, B_QDPANEL, 1024), id_b4, 1);
+        umma_commit(&S.g_full);
       }
       if (ok && nchunks > 0) {
-        ok = mbar_wait(&S.dk_read, (nchunks - 1) & 1) && mbar_wait(&S.dpre_ready, (nchunks - 1) & 1);
+        ok = pipe_wait(&S.dk_read, (nchunks - 1) & 1, ab, err, 2) &&
+             pipe_wait(&S.dpre_ready, (nchunks - 1) & 1, ab, err, 2);
         if (ok) {
           tc_fence_after();
           cw(nchunks - 1);
         }
-      }
-      if (!ok) {
-        atomicOr(err, 2);
-        S.abort = 1;
       }
       umma_commit(&S.mma_done);
       mbar_wait(&S.mma_done, 0);
@@ -316,11 +302,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     }
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1, c = nchunks - 1 - i;
-      const bool ok = mbar_wait(&S.full[s], (i >> 1) & 1);
-      if (nbar_any(2, 64, !ok)) {
-        if (at == 0) { atomicOr(err, 4); S.abort = 1; }
-        break;
-      }
+      pipe_wait(&S.full[s], (i >> 1) & 1, ab, err, 4);
       const uint32_t kt = sbase + s * B_STAGE + B_OFF_K;
       const int valid = min(B_BT, sq.len - c * B_BT);
       if (valid < B_BT) {
@@ -342,11 +324,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         m0v -= acc0;
         m1v -= acc1;
       }
-      const bool ok2 = (i < 2) || mbar_wait(&S.m_free[s], ((i - 2) >> 1) & 1);
-      if (nbar_any(2, 64, !ok2)) {
-        if (at == 0) { atomicOr(err, 8); S.abort = 1; }
-        break;
-      }
+      if (i >= 2) pipe_wait(&S.m_free[s], ((i - 2) >> 1) & 1, ab, err, 8);
       S.m_buf[s][2 * at] = m0v;
       S.m_buf[s][2 * at + 1] = m1v;
       nbar_sync(2, 64);
@@ -361,33 +339,40 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     const int g = et >> 7;
     const int qd = warp & 3;
     const int r = 32 * qd + lane;
+    const int pair = 3 + qd;                          // warps qd+4 and qd+8 share TMEM lanes
+    const int tgrp = 7 + (qd & 1);                    // z rows t and dq rows t of the same tokens
     const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
     const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
                    sR = sbase + B_OFF_R;
+    const bool dside = r < 64;                        // lanes 0-63: D / z rows, 64-127: A / dq rows
+    const int t = dside ? r : r - 64;
+    // relation of this warp's 32 rows t with this half's 32 columns j of [D ; A]
+    const bool cols_below = 32 * g + 31 < (t & ~31);
+    const bool cols_above = 32 * g > (t | 31);
     float v[64];
     // initial TMEM: C = C_T, G = dC_T, [carry | dW] = [dm_T | 0]
+    {
+      const float4* src = reinterpret_cast<const float4*>(a.state_cov + (st_base + r) * 128 + 64 * g);
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int col0 = 64 * g + 32 * hf;
-      const float4* src = reinterpret_cast<const float4*>(a.state_cov + (st_base + r) * 128 + col0);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const float4 f = src[i];
         v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
       }
-      tmem_st32(lrow + T_C + col0, v);
+      tmem_st32(lrow + T_C + 64 * g, v);
+      tmem_st32(lrow + T_C + 64 * g + 32, v + 32);
       if (a.dfinal_cov) {
-        const float4* d4 = reinterpret_cast<const float4*>(a.dfinal_cov + (st_base + r) * 128 + col0);
+        const float4* d4 = reinterpret_cast<const float4*>(a.dfinal_cov + (st_base + r) * 128 + 64 * g);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 16; ++i) {
           const float4 f = d4[i];
           v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < 64; ++i) v[i] = 0.f;
       }
-      tmem_st32(lrow + T_G + col0, v);
+      tmem_st32(lrow + T_G + 64 * g, v);
+      tmem_st32(lrow + T_G + 64 * g + 32, v + 32);
     }
     if (g == 0) {
 #pragma unroll
@@ -400,8 +385,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     fence_async_smem();
     tmem_st_wait();
     tc_fence_before();
-    nbar_sync(1, 256);
-    if (et == 0) mbar_arrive(&S.tinit);
+    warp_arrive(&S.tinit);
     float db_acc = 0.f;
 
     for (int i = 0; i < nchunks; ++i) {
@@ -409,31 +393,21 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const int t0 = c * B_BT;
       const int valid = min(B_BT, sq.len - t0);
       const uint32_t st = sbase + s * B_STAGE;
-      bool ok;
-      // ---------------- G (after this chunk) -> bf16 operand
-      ok = (i == 0) || mbar_wait(&S.g_full, (i - 1) & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 16); S.abort = 1; } break; }
+      const bool tv = t < valid;
+      // ---------------- G (after this chunk) -> bf16 operand of B3
+      if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
       tc_fence_after();
-      tmem_ld32(lrow + T_G + 64 * g, v);
-      tmem_ld32(lrow + T_G + 64 * g + 32, v + 32);
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        st_shared_v4(sG + g * 16384 + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
-                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
-                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+      tmem_ld64(lrow + T_G + 64 * g, v);
+      store_panel_row<AB16>(sG + g * 16384, r, v);
       fence_async_smem();
       tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.gconv);
+      warp_arrive(&S.gconv);
 
       // ---------------- E1: P2, tril(A), P4, dZ, R columns
-      ok = mbar_wait(&S.da_full, i & 1) && mbar_wait(&S.m_ready[s], (i >> 1) & 1) &&
-           (i == 0 || mbar_wait(&S.cw_done, (i - 1) & 1));
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 32); S.abort = 1; } break; }
+      pipe_wait(&S.da_full, i & 1, ab, err, 32);
+      pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);
+      if (i >= 1) pipe_wait(&S.cw_done, (i - 1) & 1, ab, err, 32);
       tc_fence_after();
-      const bool dside = r < 64;
-      const int t = dside ? r : r - 64;
-      const bool tv = t < valid;
       float lamv = 0.f, sv = 0.f;
       if (tv) {
         const float2 ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
@@ -445,10 +419,14 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tmem_ld32(lrow + T_DA + 32 * g, v);
       const float* mp = S.m_buf[s];
       if (dside) {
-        // w partial: sum_{j <= t} D[t][j] over my 32 columns + m_prev . dqc_t over my 64 dims
         float wp = 0.f;
+        if (cols_below) {
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) wp += (32 * g + jj <= t) ? v[jj] : 0.f;
+          for (int jj = 0; jj < 32; ++jj) wp += v[jj];
+        } else if (!cols_above) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) wp += (32 * g + jj <= t) ? v[jj] : 0.f;
+        }
         if (sub_mean) {
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
@@ -459,84 +437,73 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           }
         }
         S.wpart[g][t] = wp;
-      } else {
-        // tril(A) rows and P4 need only this thread's data; dZ = -alpha dqc for my 64 dims
-        const float beta = sub_mean ? lamv * sv * ipos * ipos : 0.f;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t am[4], p4[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int jj = 8 * q4 + 2 * e2, j = 32 * g + jj;
-            const float a0 = j <= t ? v[jj] : 0.f, a1 = j + 1 <= t ? v[jj + 1] : 0.f;
-            am[e2] = pack2<AB16>(a0, a1);
-            const float p0 = (j <= t && tv) ? beta - alpha * v[jj] : 0.f;
-            const float p1 = (j + 1 <= t && tv) ? beta - alpha * v[jj + 1] : 0.f;
-            p4[e2] = pack2<AB16>(p0, p1);
-          }
-          st_shared_v4(sAP + sw128(t, 4 * g + q4), am[0], am[1], am[2], am[3]);
-          st_shared_v4(sP4 + sw128(t, 4 * g + q4), p4[0], p4[1], p4[2], p4[3]);
-        }
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          float f[8];
-          ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
-          st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), pack2<AB16>(-alpha * f[0], -alpha * f[1]),
-                       pack2<AB16>(-alpha * f[2], -alpha * f[3]), pack2<AB16>(-alpha * f[4], -alpha * f[5]),
-                       pack2<AB16>(-alpha * f[6], -alpha * f[7]));
-        }
-        if (g == 0) st_shared_u16(sR + 2048 + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(tv ? beta : 0.f));
-      }
-      nbar_sync(1, 256);
-      if (dside) {
+        nbar_sync(pair, 64);
         const float w = S.wpart[0][t] + S.wpart[1][t];
-        const float ds = sub_mean ? lamv * w * ipos * ipos : 0.f;
+        const float ds = (sub_mean && tv) ? lamv * w * ipos * ipos : 0.f;
+        const float na = tv ? -alpha : 0.f;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           uint32_t p2[4];
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
             const int jj = 8 * q4 + 2 * e2, j = 32 * g + jj;
-            const float p0 = (j <= t && tv) ? ds - alpha * v[jj] : 0.f;
-            const float p1 = (j + 1 <= t && tv) ? ds - alpha * v[jj + 1] : 0.f;
+            const float p0 = (j <= t) ? fmaf(na, v[jj], ds) : 0.f;
+            const float p1 = (j + 1 <= t) ? fmaf(na, v[jj + 1], ds) : 0.f;
             p2[e2] = pack2<AB16>(p0, p1);
           }
           st_shared_v4(sAP + 8192 + sw128(t, 4 * g + q4), p2[0], p2[1], p2[2], p2[3]);
         }
         if (g == 0) {
           S.w[t] = w;
-          S.ds[t] = tv ? ds : 0.f;
-          st_shared_u16(sR + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(tv ? ds : 0.f));
+          S.ds[t] = ds;
+          st_shared_u16(sR + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(ds));
         }
+      } else {
+        const float beta = (sub_mean && tv) ? lamv * sv * ipos * ipos : 0.f;
+        const float na = tv ? -alpha : 0.f;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t am[4], p4[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int jj = 8 * q4 + 2 * e2, j = 32 * g + jj;
+            am[e2] = pack2<AB16>(j <= t ? v[jj] : 0.f, j + 1 <= t ? v[jj + 1] : 0.f);
+            p4[e2] = pack2<AB16>(j <= t ? fmaf(na, v[jj], beta) : 0.f, j + 1 <= t ? fmaf(na, v[jj + 1], beta) : 0.f);
+          }
+          st_shared_v4(sAP + sw128(t, 4 * g + q4), am[0], am[1], am[2], am[3]);
+          st_shared_v4(sP4 + sw128(t, 4 * g + q4), p4[0], p4[1], p4[2], p4[3]);
+        }
+        // dZ = -alpha dqc, packed
+        const uint32_t na2 = pack2<AB16>(na, na);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
+          st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), mul2<AB16>(d.x, na2), mul2<AB16>(d.y, na2),
+                       mul2<AB16>(d.z, na2), mul2<AB16>(d.w, na2));
+        }
+        if (g == 0) st_shared_u16(sR + 2048 + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
       }
       fence_async_smem();
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.pdone);
+      warp_arrive(&S.pdone);
 
-      // ---------------- C_prev -> bf16 operand
-      ok = mbar_wait(&S.c_full, i & 1) && (i == 0 || mbar_wait(&S.cprev_free, (i - 1) & 1));
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 64); S.abort = 1; } break; }
+      // ---------------- C_prev -> bf16 operand of B2
+      pipe_wait(&S.c_full, i & 1, ab, err, 64);
       tc_fence_after();
-      tmem_ld32(lrow + T_C + 64 * g, v);
-      tmem_ld32(lrow + T_C + 64 * g + 32, v + 32);
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        st_shared_v4(sC + g * 16384 + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
-                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
-                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+      tmem_ld64(lrow + T_C + 64 * g, v);
+      tc_fence_before();
+      warp_arrive(&S.c_read);
+      if (i >= 1) pipe_wait(&S.cprev_free, (i - 1) & 1, ab, err, 64);
+      store_panel_row<AB16>(sC + g * 16384, r, v);
       fence_async_smem();
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.cconv);
+      warp_arrive(&S.cconv);
 
-      // ---------------- E2: dlambda (z side) and dq (dq side)
-      ok = mbar_wait(&S.zq_full, i & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 128); S.abort = 1; } break; }
+      // ---------------- E2: dlambda (z rows) and dq (dq rows)
+      pipe_wait(&S.zq_full, i & 1, ab, err, 128);
       tc_fence_after();
-      tmem_ld32(lrow + T_ZQ + 64 * g, v);
-      tmem_ld32(lrow + T_ZQ + 64 * g + 32, v + 32);
-      if (dside) {  // lanes 0-63 hold z
+      tmem_ld64(lrow + T_ZQ + 64 * g, v);
+      tc_fence_before();
+      warp_arrive(&S.zq_free);
+      if (dside) {
         float up = 0.f;
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
@@ -546,68 +513,63 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           for (int e2 = 0; e2 < 8; ++e2) up = fmaf(f[e2], v[8 * cc + e2], up);
         }
         S.upart[g][t] = up;
+        nbar_sync(pair, 64);
+        if (g == 0) {
+          const float u = S.upart[0][t] + S.upart[1][t];
+          float dl = -u * ipos;
+          if (sub_mean) dl += sv * S.w[t] * ipos * ipos;
+          float dp = 0.f;
+          if (gate) dp = tv ? dl * lamv * (1.f - lamv) : 0.f;
+          else if (tv && a.dlam) a.dlam[(sq.bos + t0 + t) * H + h] = dl;
+          S.dpre[t] = dp;
+          st_shared_u16(sR + sw128(1, t >> 3) + (t & 7) * 2, to16<AB16>(dp));
+          db_acc += dp;
+        }
       }
-      nbar_sync(1, 256);
-      if (dside && g == 0) {
-        const float u = S.upart[0][t] + S.upart[1][t];
-        float dl = -u * ipos;
-        if (sub_mean) dl += sv * S.w[t] * ipos * ipos;
-        const int64_t tok = (sq.bos + t0 + t) * H + h;
-        float dp = 0.f;
-        if (gate) dp = tv ? dl * lamv * (1.f - lamv) : 0.f;
-        else if (tv && a.dlam) a.dlam[tok] = dl;
-        S.dpre[t] = dp;
-        st_shared_u16(sR + sw128(1, t >> 3) + (t & 7) * 2, to16<AB16>(dp));
-        db_acc += dp;
-      }
-      if (gate) nbar_sync(1, 256);
-      if (!dside) {  // lanes 64-127 hold the dq accumulator
+      if (gate) nbar_sync(tgrp, 128);  // dpre of these tokens is in S.dpre
+      if (!dside) {
         const float ds = S.ds[t];
         const float dp = gate ? S.dpre[t] : 0.f;
         uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-          float f[8];
-          ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
+          const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
+          const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
           uint32_t o[4];
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
-            const int d0 = 64 * g + 8 * cc + 2 * e2;
-            float x0 = f[2 * e2] + ds * mp[d0] + v[8 * cc + 2 * e2];
-            float x1 = f[2 * e2 + 1] + ds * mp[d0 + 1] + v[8 * cc + 2 * e2 + 1];
+            const int jj = 8 * cc + 2 * e2, d0 = 64 * g + jj;
+            float x0 = fmaf(ds, mp[d0], v[jj]);
+            float x1 = fmaf(ds, mp[d0 + 1], v[jj + 1]);
             if (gate) {
               x0 = fmaf(dp, S.wh[d0], x0);
               x1 = fmaf(dp, S.wh[d0 + 1], x1);
             }
-            o[e2] = pack2<AB16>(x0, x1);
+            const float2 f = unpack2<AB16>(dw[e2]);
+            o[e2] = pack2<AB16>(f.x + x0, f.y + x1);
           }
           if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       fence_async_smem();
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) {
-        mbar_arrive(&S.zq_free);
-        mbar_arrive(&S.dpre_ready);
-        mbar_arrive(&S.m_free[s]);
-      }
+      warp_arrive(&S.dpre_ready);
+      warp_arrive(&S.m_free[s]);
 
       // ---------------- E3: dk = dk^T + carry, staged through the K tile
-      ok = mbar_wait(&S.dk_full, i & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 256); S.abort = 1; } break; }
+      pipe_wait(&S.dk_full, i & 1, ab, err, 256);
       tc_fence_after();
       tmem_ld32(lrow + T_DA + 32 * g, v);
-      const float carry = tmem_ld1(lrow + T_CW);
+      float cwv[2];
+      tmem_ld2f(lrow + T_CW, cwv);
+      tc_fence_before();
+      warp_arrive(&S.dk_read);
       {
         const uint32_t kpanel = st + B_OFF_K + (r >> 6) * B_KPANEL + ((r & 7) * 2);
         const uint32_t rc = (r & 63) >> 3;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + carry));
+        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + cwv[0]));
       }
-      tc_fence_before();
       nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.dk_read);
 #pragma unroll
       for (int k4 = 0; k4 < 4; ++k4) {
         const int qid = et + 256 * k4;             // 16-byte chunk id: row (64) x panel (2) x chunk (8)
@@ -618,29 +580,25 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         }
       }
       fence_async_smem();
-      nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.empty[s]);
+      warp_arrive(&S.empty[s]);
     }
     // ---------------- per-document outputs
-    if (!nbar_any(1, 256, *(volatile int*)&S.abort != 0)) {
-      const bool okf = (nchunks == 0) || (mbar_wait(&S.g_full, (nchunks - 1) & 1) &&
-                                          mbar_wait(&S.cw_done, (nchunks - 1) & 1));
-      if (!nbar_any(1, 256, !okf)) {
-        tc_fence_after();
-        if (a.dinitial_cov) {
-          tmem_ld32(lrow + T_G + 64 * g, v);
-          tmem_ld32(lrow + T_G + 64 * g + 32, v + 32);
-          float4* dst = reinterpret_cast<float4*>(a.dinitial_cov + (st_base + r) * 128 + 64 * g);
+    if (nchunks > 0) {
+      pipe_wait(&S.g_full, (nchunks - 1) & 1, ab, err, 512);
+      pipe_wait(&S.cw_done, (nchunks - 1) & 1, ab, err, 512);
+    }
+    tc_fence_after();
+    if (a.dinitial_cov) {
+      tmem_ld64(lrow + T_G + 64 * g, v);
+      float4* dst = reinterpret_cast<float4*>(a.dinitial_cov + (st_base + r) * 128 + 64 * g);
 #pragma unroll
-          for (int k4 = 0; k4 < 16; ++k4) dst[k4] = make_float4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]);
-        }
-        float cwv[2];
-        tmem_ld2f(lrow + T_CW, cwv);
-        if (g == 0 && a.dinitial_mean) a.dinitial_mean[st_base + r] = cwv[0];
-        if (g == 0 && gate) gate_part[((int64_t)n * H + h) * 129 + r] = cwv[1];
-      } else if (et == 0) {
-        atomicOr(err, 512);
-      }
+      for (int k4 = 0; k4 < 16; ++k4) dst[k4] = make_float4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]);
+    }
+    {
+      float cwv[2];
+      tmem_ld2f(lrow + T_CW, cwv);
+      if (g == 0 && a.dinitial_mean) a.dinitial_mean[st_base + r] = cwv[0];
+      if (g == 0 && gate) gate_part[((int64_t)n * H + h) * 129 + r] = cwv[1];
     }
     if (gate) {
       db_acc = warp_sum(db_acc);

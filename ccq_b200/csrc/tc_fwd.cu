@@ -2,21 +2,23 @@
 //
 // One CTA per (document, head) walks the document in chunks of BT = 128 tokens.  The covariance
 // state C (128 x 128 fp32) lives in TMEM for the whole document and is never written to HBM, so
-// the kernel reads q and k once and writes q_clean once.  Per chunk (Q, K = 128 x 128 tiles):
-//   F1  A  = Q [K ; m_hi ; m_lo ; w_hi ; w_lo]^T     (N = 144: q k_j^T, q.m_prev, and q.w for the gate)
-//   F3  C += K^T K                                   (the state update, fp32 accumulate in TMEM)
+// the kernel reads q and k once and writes q_clean once.  Per chunk (Q, K = 128 x 128 tiles; the K
+// tile carries four extra rows m_hi, m_lo, w_hi, w_lo after its 128 keys):
+//   F1  A  = Q [K ; m_hi ; m_lo ; w_hi ; w_lo]^T        (N = 144: q k_j^T, q.m_prev, q.w for the gate)
+//   F3  C += K^T K                                      (the state update, fp32 accumulate in TMEM)
 //   F2a Z  = Q bf16(C_prev)
-//   F2b Z += P' K,  P'[t][j] = (A[t][j] - s_t / pos_t) [j <= t]
-// so that Z_t = z_t - (s_t / pos_t)(m_t - m_prev) and the epilogue only adds the rank-1 term:
-//   q_clean_t = q_t - (lambda_t / pos_t) (Z_t - (s_t / pos_t) m_prev)
-// which is the reference's q_t - lambda_t (z_t / pos_t - s_t m_t / pos_t^2)
-// (ccq/ops/common/fused_read.py:11-16, kernel at :86-174).
+//   F2b Z += [P' | -sp -sp] [K ; m_hi ; m_lo]           (K-dim 144: the rank-1 mean term rides along)
+// with P'[t][j] = (A[t][j] - sp_t)[j <= t], sp_t = s_t / pos_t, s_t = q_t . m_t, so that
+//   Z_t = z_t - sp_t m_t   and   q_clean_t = q_t - (lambda_t / pos_t) Z_t,
+// the reference's q_t - lambda_t (z_t / pos_t - s_t m_t / pos_t^2) (ccq/ops/common/fused_read.py:11-16,
+// kernel at :86-174).
 //
 // Warp roles (384 threads): warp 0 issues TMA loads, warp 1 allocates TMEM and issues every MMA
 // from one thread, warps 2-3 ("aux") keep the running key sum m and patch the K tile's extra rows,
-// warps 4-11 ("epilogue", two warpgroups splitting the 128 columns) turn A into P', convert C to
-// the bf16 operand for the next chunk and write q_clean.  Every mbarrier wait is bounded; on a
-// timeout the CTA records an error in the workspace and unwinds.
+// warps 4-11 ("epilogue", two warpgroups splitting the 128 columns; warps w and w + 4 share TMEM
+// lanes) turn A into P', convert C to the bf16 operand of the next chunk and write q_clean.  Each
+// epilogue warp releases a TMEM buffer as soon as it holds the values in registers.  Every
+// mbarrier wait is bounded; on a timeout the CTA records an error in the workspace and unwinds.
 #include "args.h"
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -37,16 +39,16 @@ constexpr uint32_t F_KTILE = 2 * F_KPANEL;
 constexpr uint32_t F_OFF_Q = 0;                       // two stages
 constexpr uint32_t F_OFF_K = 2 * F_QTILE;             // two stages
 constexpr uint32_t F_OFF_C = F_OFF_K + 2 * F_KTILE;   // bf16 C_prev (MN-major B operand)
-constexpr uint32_t F_OFF_P = F_OFF_C + F_QTILE;       // P' (K-major A operand)
-constexpr uint32_t F_OFF_SMALL = F_OFF_P + F_QTILE;   // 204800
+constexpr uint32_t F_OFF_P = F_OFF_C + F_QTILE;       // [P' | mean columns] (K-major A operand, 3 panels)
+constexpr uint32_t F_OFF_SMALL = F_OFF_P + 3 * F_QPANEL;
 constexpr uint32_t T_C = 0, T_A = 128, T_Z = 272;      // TMEM columns: C (128), A (144), Z (128)
+constexpr int EPI_WARPS = 8;
 
 struct FwdSmall {
-  float m_buf[2][128];
-  float s_part[2][128];
-  float lam[128], ipos[128], sp[128];
-  uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
-  uint64_t a_full, a_free, cconv, cprev_free, c_full, pready, z_full, z_free, mma_done;
+  float xchg[2][128];
+  float cf[128];
+  uint64_t full[2], kready[2], empty[2];
+  uint64_t a_full, a_free, c_read, cconv, cprev_free, c_full, pready, z_full, z_free, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -56,20 +58,6 @@ static_assert(F_SMEM <= 232448, "forward kernel shared memory");
 __device__ __forceinline__ void nbar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
-// every thread of the named-barrier group gets the OR of v
-__device__ __forceinline__ bool nbar_any(int id, int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -126,6 +114,14 @@ __device__ __forceinline__ uint32_t to16(float x) {
 }
 
 template <int AB16>
+__device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const float* v) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+    st_shared_v4(panel + sw128(row, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]), pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]),
+                 pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]), pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+}
+
+template <int AB16>
 __global__ void __launch_bounds__(F_THREADS, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, CleanArgs a,
                   int* err) {
@@ -146,18 +142,17 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.kready[i], 1);
-      mbar_init(&S.empty[i], 3);
-      mbar_init(&S.m_ready[i], 1);
-      mbar_init(&S.m_free[i], 1);
+      mbar_init(&S.empty[i], 2 + EPI_WARPS);
     }
     mbar_init(&S.a_full, 1);
-    mbar_init(&S.a_free, 1);
-    mbar_init(&S.cconv, 1);
+    mbar_init(&S.a_free, EPI_WARPS);
+    mbar_init(&S.c_read, EPI_WARPS);
+    mbar_init(&S.cconv, EPI_WARPS);
     mbar_init(&S.cprev_free, 1);
     mbar_init(&S.c_full, 1);
-    mbar_init(&S.pready, 1);
+    mbar_init(&S.pready, EPI_WARPS);
     mbar_init(&S.z_full, 1);
-    mbar_init(&S.z_free, 1);
+    mbar_init(&S.z_free, EPI_WARPS);
     mbar_init(&S.mma_done, 1);
     S.abort = 0;
     fence_barrier_init();
@@ -167,6 +162,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = S.tmem_base;
+  volatile int* ab = &S.abort;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -176,12 +172,8 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
         const int s = c & 1;
-        if (c >= 2 && !mbar_wait(&S.empty[s], ((c - 2) >> 1) & 1)) {
-          atomicOr(err, 1);
-          S.abort = 1;
-          break;
-        }
-        if (*(volatile int*)&S.abort) break;
+        if (c >= 2 && !pipe_wait(&S.empty[s], ((c - 2) >> 1) & 1, ab, err, 1)) break;
+        if (*ab) break;
         mbar_arrive_expect_tx(&S.full[s], 2 * F_QTILE);
         const int row = (int)(sq.bos + (int64_t)c * F_BT);
         uint8_t* q_dst = sm + F_OFF_Q + s * F_QTILE;
@@ -199,14 +191,14 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_a = idesc_f16(128, 144, AB16, 0, 0);
-      const uint32_t id_z1 = idesc_f16(128, 128, AB16, 0, 1);
+      const uint32_t id_z = idesc_f16(128, 128, AB16, 0, 1);
       const uint32_t id_c = idesc_f16(128, 128, AB16, 1, 1);
       const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
       bool ok = true;
       for (int c = 0; c < nchunks && ok; ++c) {
         const int s = c & 1;
         const uint32_t sQ = sbase + F_OFF_Q + s * F_QTILE, sK = sbase + F_OFF_K + s * F_KTILE;
-        ok = mbar_wait(&S.kready[s], (c >> 1) & 1) && (c == 0 || mbar_wait(&S.a_free, (c - 1) & 1));
+        ok = pipe_wait(&S.kready[s], (c >> 1) & 1, ab, err, 2) && (c == 0 || pipe_wait(&S.a_free, (c - 1) & 1, ab, err, 2));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -214,34 +206,30 @@ __global__ void __launch_bounds__(F_THREADS, 1)
           umma(tbase + T_A, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
                sdesc(sK + (ks >> 2) * F_KPANEL + (ks & 3) * 32, 16, 1024), id_a, ks > 0);
         umma_commit(&S.a_full);
-        ok = mbar_wait(&S.cconv, c & 1);
+        ok = pipe_wait(&S.c_read, c & 1, ab, err, 2);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma(tbase + T_C, sdesc(sK + ks * 2048, F_KPANEL, 1024), sdesc(sK + ks * 2048, F_KPANEL, 1024), id_c, 1);
         umma_commit(&S.c_full);
-        ok = (c == 0 || mbar_wait(&S.z_free, (c - 1) & 1));
+        ok = pipe_wait(&S.cconv, c & 1, ab, err, 2) && (c == 0 || pipe_wait(&S.z_free, (c - 1) & 1, ab, err, 2));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma(tbase + T_Z, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
-               sdesc(sC + ks * 2048, F_QPANEL, 1024), id_z1, ks > 0);
+               sdesc(sC + ks * 2048, F_QPANEL, 1024), id_z, ks > 0);
         umma_commit(&S.cprev_free);
-        ok = mbar_wait(&S.pready, c & 1);
+        ok = pipe_wait(&S.pready, c & 1, ab, err, 2);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
+        for (int ks = 0; ks < 9; ++ks)
           umma(tbase + T_Z, sdesc(sP + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
-               sdesc(sK + ks * 2048, F_KPANEL, 1024), id_z1, 1);
+               sdesc(sK + ks * 2048, F_KPANEL, 1024), id_z, 1);
         umma_commit(&S.z_full);
         umma_commit(&S.empty[s]);
-      }
-      if (!ok) {
-        atomicOr(err, 2);
-        S.abort = 1;
       }
       // TMEM is freed only after every issued MMA has completed
       umma_commit(&S.mma_done);
@@ -258,8 +246,6 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       m0v = a.initial_mean[st_base + 2 * at];
       m1v = a.initial_mean[st_base + 2 * at + 1];
     }
-    S.m_buf[0][2 * at] = m0v;
-    S.m_buf[0][2 * at + 1] = m1v;
     uint32_t wh = 0, wl = 0;
     if (gate) {
       float r0, r1;
@@ -273,15 +259,9 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       for (uint32_t row = 130; row < F_KROWS; ++row)
         st_shared_u32(kb + sw128(row, ch) + cb, row == 130 ? wh : (row == 131 ? wl : 0u));
     }
-    nbar_sync(2, 64);
-    if (at == 0) mbar_arrive(&S.m_ready[0]);
     for (int c = 0; c < nchunks; ++c) {
       const int s = c & 1;
-      const bool ok = mbar_wait(&S.full[s], (c >> 1) & 1);
-      if (nbar_any(2, 64, !ok)) {
-        if (at == 0) { atomicOr(err, 4); S.abort = 1; }
-        break;
-      }
+      pipe_wait(&S.full[s], (c >> 1) & 1, ab, err, 4);
       const uint32_t kt = sbase + F_OFF_K + s * F_KTILE;
       const int valid = min(F_BT, sq.len - c * F_BT);
       if (valid < F_BT) {  // keys past the end of the document belong to the next one: zero them
@@ -311,18 +291,8 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         m0v += acc0;
         m1v += acc1;
       }
-      bool ok2 = (c == 0) || mbar_wait(&S.m_free[(c - 1) & 1], ((c - 1) >> 1) & 1);
-      if (nbar_any(2, 64, !ok2)) {
-        if (at == 0) { atomicOr(err, 8); S.abort = 1; }
-        break;
-      }
-      S.m_buf[(c + 1) & 1][2 * at] = m0v;
-      S.m_buf[(c + 1) & 1][2 * at + 1] = m1v;
       nbar_sync(2, 64);
-      if (at == 0) {
-        mbar_arrive(&S.m_ready[(c + 1) & 1]);
-        mbar_arrive(&S.empty[s]);
-      }
+      if (at == 0) mbar_arrive(&S.empty[s]);
     }
     if (sub_mean && a.final_mean) {
       a.final_mean[st_base + 2 * at] = m0v;
@@ -334,154 +304,138 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     const int g = et >> 7;                        // column half
     const int qd = warp & 3;                      // TMEM lane quadrant of this warp
     const int r = 32 * qd + lane;                 // token (A, Z) or state row (C)
+    const int pair = 3 + qd;                      // named barrier shared by warps qd+4 and qd+8
     const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
     const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
     const float gate_b = gate ? a.gate_b[h] : 0.f;
+    // diagonal relation of this warp's 32 rows with this half's 64 columns
+    const bool cols_all_below = 64 * g + 63 < 32 * qd;    // every column j < every row t
+    const bool cols_all_above = 64 * g > 32 * qd + 31;    // every column j > every row t
     float v[64];
     // initial state -> TMEM C and the bf16 operand for chunk 0
+    if (a.initial_cov) {
+      const float4* src = reinterpret_cast<const float4*>(a.initial_cov + (st_base + r) * 128 + 64 * g);
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int col0 = 64 * g + 32 * hf;
-      if (a.initial_cov) {
-        const float4* src = reinterpret_cast<const float4*>(a.initial_cov + (st_base + r) * 128 + col0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 f = src[i];
-          v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      for (int i = 0; i < 16; ++i) {
+        const float4 f = src[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
       }
-      tmem_st32(lrow + T_C + col0, v);
-      if (nchunks == 0 && a.final_cov) {
-        float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + col0);
+    } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      }
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc)
-        st_shared_v4(sC + g * F_QPANEL + sw128(r, 4 * hf + cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
-                     pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
-                     pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+      for (int i = 0; i < 64; ++i) v[i] = 0.f;
     }
+    tmem_st32(lrow + T_C + 64 * g, v);
+    tmem_st32(lrow + T_C + 64 * g + 32, v + 32);
+    if (nchunks == 0 && a.final_cov) {
+      float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * g);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    store_panel_row<AB16>(sC + g * F_QPANEL, r, v);
+    // constant part of the mean columns of P' (columns 136..143 stay zero)
+    st_shared_v4(sP + 2 * F_QPANEL + sw128(r, 1 + g), 0u, 0u, 0u, 0u);
     tmem_st_wait();
     fence_async_smem();
     tc_fence_before();
-    nbar_sync(1, 256);
-    if (et == 0) mbar_arrive(&S.cconv);
+    warp_arrive(&S.c_read);
+    warp_arrive(&S.cconv);
 
     for (int c = 0; c < nchunks; ++c) {
       const int s = c & 1;
       const int t0 = c * F_BT;
       const int valid = min(F_BT, sq.len - t0);
       const int t = r;
-      // ---------------- P' = (A - s/pos) on and below the diagonal
-      bool ok = mbar_wait(&S.a_full, c & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 16); S.abort = 1; } break; }
+      // ---------------- P' = (A - s/pos) on and below the diagonal, plus the mean columns
+      pipe_wait(&S.a_full, c & 1, ab, err, 16);
       tc_fence_after();
-      tmem_ld32(lrow + T_A + 64 * g, v);
-      tmem_ld32(lrow + T_A + 64 * g + 32, v + 32);
+      tmem_ld64(lrow + T_A + 64 * g, v);
       float ext[4] = {0.f, 0.f, 0.f, 0.f};
       if (g == 0) tmem_ld4(lrow + T_A + 128, ext);
+      tc_fence_before();
+      warp_arrive(&S.a_free);
       const float ipos = 1.f / position_of(t0 + t, a.position_offset);
       float part = 0.f;
+      if (cols_all_below) {
 #pragma unroll
-      for (int jj = 0; jj < 64; ++jj) part += (64 * g + jj <= t) ? v[jj] : 0.f;
+        for (int jj = 0; jj < 64; ++jj) part += v[jj];
+      } else if (!cols_all_above) {
+#pragma unroll
+        for (int jj = 0; jj < 64; ++jj) part += (64 * g + jj <= t) ? v[jj] : 0.f;
+      }
+      float lamv = 0.f;
       if (g == 0) {
         part += ext[0] + ext[1];
-        float lamv;
         if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
         else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
-        S.lam[t] = lamv;
-        S.ipos[t] = ipos;
+        S.cf[t] = lamv * ipos;
       }
-      S.s_part[g][t] = part;
-      nbar_sync(1, 256);
-      const float st = sub_mean ? S.s_part[0][t] + S.s_part[1][t] : 0.f;
-      const float sp = st * ipos;
-      if (g == 0) {
-        S.sp[t] = sp;
-        if (a.token_aux && t < valid) {
+      // pair exchange of the partial row sums (warps qd+4 and qd+8 hold the same rows)
+      S.xchg[g][t] = part;
+      nbar_sync(pair, 64);
+      {
+        const float st = sub_mean ? S.xchg[0][t] + S.xchg[1][t] : 0.f;
+        const float sp = st * ipos;
+        if (g == 0 && a.token_aux && t < valid) {
           float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
-          *aux = make_float2(S.lam[t], st);
+          *aux = make_float2(lamv, st);
         }
-      }
+        if (cols_all_above) {
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint32_t w[4];
+          for (int cc = 0; cc < 8; ++cc) st_shared_v4(sP + g * F_QPANEL + sw128(t, cc), 0u, 0u, 0u, 0u);
+        } else if (cols_all_below) {
 #pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          const int j0 = 64 * g + 8 * cc + 2 * e2;
-          const float x0 = j0 <= t ? v[8 * cc + 2 * e2] - sp : 0.f;
-          const float x1 = j0 + 1 <= t ? v[8 * cc + 2 * e2 + 1] - sp : 0.f;
-          w[e2] = pack2<AB16>(x0, x1);
+          for (int i = 0; i < 64; ++i) v[i] -= sp;
+          store_panel_row<AB16>(sP + g * F_QPANEL, t, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] = (64 * g + i <= t) ? v[i] - sp : 0.f;
+          store_panel_row<AB16>(sP + g * F_QPANEL, t, v);
         }
-        st_shared_v4(sP + g * F_QPANEL + sw128(t, cc), w[0], w[1], w[2], w[3]);
+        if (g == 0) {
+          const uint32_t nsp = pack2<AB16>(-sp, -sp);
+          st_shared_v4(sP + 2 * F_QPANEL + sw128(t, 0), nsp, 0u, 0u, 0u);
+        }
       }
       fence_async_smem();
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) {
-        mbar_arrive(&S.pready);
-        mbar_arrive(&S.a_free);
-      }
+      warp_arrive(&S.pready);
       // ---------------- C after this chunk -> bf16 operand of the next chunk (or the final state)
-      ok = mbar_wait(&S.c_full, c & 1) && mbar_wait(&S.cprev_free, c & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 32); S.abort = 1; } break; }
+      pipe_wait(&S.c_full, c & 1, ab, err, 32);
       tc_fence_after();
-      tmem_ld32(lrow + T_C + 64 * g, v);
-      tmem_ld32(lrow + T_C + 64 * g + 32, v + 32);
+      tmem_ld64(lrow + T_C + 64 * g, v);
+      tc_fence_before();
+      warp_arrive(&S.c_read);
       if (c + 1 < nchunks) {
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc)
-          st_shared_v4(sC + g * F_QPANEL + sw128(r, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]),
-                       pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]), pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]),
-                       pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+        pipe_wait(&S.cprev_free, c & 1, ab, err, 64);
+        store_panel_row<AB16>(sC + g * F_QPANEL, r, v);
         fence_async_smem();
       } else if (a.final_cov) {
         float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * g);
 #pragma unroll
         for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) mbar_arrive(&S.cconv);
-      // ---------------- q_clean = q - lam/pos (Z - sp m_prev)
-      ok = mbar_wait(&S.z_full, c & 1) && mbar_wait(&S.m_ready[s], (c >> 1) & 1);
-      if (nbar_any(1, 256, !ok)) { if (et == 0) { atomicOr(err, 64); S.abort = 1; } break; }
+      warp_arrive(&S.cconv);
+      // ---------------- q_clean = q - (lambda / pos) Z
+      pipe_wait(&S.z_full, c & 1, ab, err, 128);
       tc_fence_after();
-      tmem_ld32(lrow + T_Z + 64 * g, v);
-      tmem_ld32(lrow + T_Z + 64 * g + 32, v + 32);
+      tmem_ld64(lrow + T_Z + 64 * g, v);
+      tc_fence_before();
+      warp_arrive(&S.z_free);
       {
-        const float cf = S.lam[t] * S.ipos[t];
-        const float spv = S.sp[t];
-        const float* mp = S.m_buf[s] + 64 * g;
+        const float cf = S.cf[t];
         const uint32_t qrow = sbase + F_OFF_Q + s * F_QTILE + g * F_QPANEL;
-        void* orow = (uint8_t*)a.q_clean + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2;
+        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.q_clean + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           const uint4 qv = ld_shared_v4(qrow + sw128(t, cc));
-          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int jj = 8 * cc + 2 * e2;
-            const float2 qf = unpack2<AB16>(qw[e2]);
-            const float r0 = v[jj] - spv * mp[jj];
-            const float r1 = v[jj + 1] - spv * mp[jj + 1];
-            o[e2] = pack2<AB16>(qf.x - cf * r0, qf.y - cf * r1);
-          }
-          if (t < valid) reinterpret_cast<uint4*>(orow)[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+          const uint4 o = make_uint4(sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
+                                     sub2<AB16>(qv.y, pack2<AB16>(cf * v[8 * cc + 2], cf * v[8 * cc + 3])),
+                                     sub2<AB16>(qv.z, pack2<AB16>(cf * v[8 * cc + 4], cf * v[8 * cc + 5])),
+                                     sub2<AB16>(qv.w, pack2<AB16>(cf * v[8 * cc + 6], cf * v[8 * cc + 7])));
+          if (t < valid) orow[cc] = o;
         }
       }
-      tc_fence_before();
-      nbar_sync(1, 256);
-      if (et == 0) {
-        mbar_arrive(&S.z_free);
-        mbar_arrive(&S.m_free[s]);
-        mbar_arrive(&S.empty[s]);
-      }
+      nbar_sync(pair, 64);  // both halves have read S.cf before the next chunk rewrites it
+      warp_arrive(&S.empty[s]);
     }
   }
   tc_fence_before();
