@@ -175,6 +175,7 @@ def run_ours(args, rank, world, local_rank):
 
     import ccq_b200
     from ccq_b200 import _lib, ops
+    from ccq_b200.distributed import allreduce_gate_grads
 
     device = torch.device('cuda', local_rank)
     torch.cuda.set_device(device)
@@ -201,8 +202,7 @@ def run_ours(args, rank, world, local_rank):
 
     def allreduce(dW, db):
         if world > 1:
-            dist.all_reduce(dW)
-            dist.all_reduce(db)
+            allreduce_gate_grads(dW, db)
 
     stream = torch.cuda.current_stream(device)
     for _ in range(args.warmup):
