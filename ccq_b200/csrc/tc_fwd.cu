@@ -3,7 +3,7 @@
 // One CTA per (document, head) walks the document in chunks of BT = 128 tokens.  The covariance
 // state C (128 x 128 fp32) lives in TMEM for the whole document and is never written to HBM, so
 // the kernel reads q and k once and writes q_clean once.  Per chunk (Q, K = 128 x 128 tiles; the K
-// tile carries four extra rows m_hi, m_lo, w_hi, w_lo after its 128 keys):
+// tile carries four extra rows m_hi, m_lo, w_hi, w_lo after its 128 keys, then zero rows to 144):
 //   F1  A  = Q [K ; m_hi ; m_lo ; w_hi ; w_lo]^T        (N = 144: q k_j^T, q.m_prev, q.w for the gate)
 //   F3  C += K^T K                                      (the state update, fp32 accumulate in TMEM)
 //   F2a Z  = Q bf16(C_prev)
@@ -11,14 +11,21 @@
 // with P'[t][j] = (A[t][j] - sp_t)[j <= t], sp_t = s_t / pos_t, s_t = q_t . m_t, so that
 //   Z_t = z_t - sp_t m_t   and   q_clean_t = q_t - (lambda_t / pos_t) Z_t,
 // the reference's q_t - lambda_t (z_t / pos_t - s_t m_t / pos_t^2) (ccq/ops/common/fused_read.py:11-16,
-// kernel at :86-174).
+// kernel at :86-174).  TMEM holds C (128 columns), two 144-column regions and P' (72 columns of
+// packed 16-bit values, the A operand of F2b); chunk i uses region i % 2 first for its scores A_i
+// and then, once they are read, for Z_i, so the scores of chunk i+1 and the output of chunk i are in
+// flight together.  q_clean is staged in shared memory and written by TMA bulk stores.
 //
-// Warp roles (384 threads): warp 0 issues TMA loads, warp 1 allocates TMEM and issues every MMA
-// from one thread, warps 2-3 ("aux") keep the running key sum m and patch the K tile's extra rows,
-// warps 4-11 ("epilogue", two warpgroups splitting the 128 columns; warps w and w + 4 share TMEM
-// lanes) turn A into P', convert C to the bf16 operand of the next chunk and write q_clean.  Each
-// epilogue warp releases a TMEM buffer as soon as it holds the values in registers.  Every
-// mbarrier wait is bounded; on a timeout the CTA records an error in the workspace and unwinds.
+// Warp roles (640 threads):
+//   warp 0      TMA loads of the Q / K tiles (two stages);
+//   warp 1      TMEM allocation and every MMA, from one thread that issues whichever of the four MMA
+//               groups has its inputs ready (the groups of neighbouring chunks overlap);
+//   warps 2-3   running key sum m: the m rows of the K tile and the fp32 m_prev of each chunk;
+//   warps 4-11  "score" group: A -> P' (two warps per TMEM lane quadrant, 64 columns each), lambda;
+//   warps 12-19 "output" group: C -> bf16 operand of the next chunk, Z -> q_clean (one thread issues
+//               the bulk store of each full chunk; a document's last, partial chunk is written with
+//               plain stores so no row of the next document is touched).
+// Every mbarrier wait is bounded; on a timeout the CTA records an error in the workspace and unwinds.
 #include "args.h"
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -29,7 +36,7 @@ namespace ccq {
 namespace {
 using namespace tc;
 
-constexpr int F_THREADS = 384;
+constexpr int F_THREADS = 640;
 constexpr int F_BT = 128;
 constexpr uint32_t F_QPANEL = 16384;                  // 128 rows x 128 B
 constexpr uint32_t F_QTILE = 2 * F_QPANEL;            // 128 x 128 bf16
@@ -39,16 +46,18 @@ constexpr uint32_t F_KTILE = 2 * F_KPANEL;
 constexpr uint32_t F_OFF_Q = 0;                       // two stages
 constexpr uint32_t F_OFF_K = 2 * F_QTILE;             // two stages
 constexpr uint32_t F_OFF_C = F_OFF_K + 2 * F_KTILE;   // bf16 C_prev (MN-major B operand)
-constexpr uint32_t F_OFF_P = F_OFF_C + F_QTILE;       // [P' | mean columns] (K-major A operand, 3 panels)
-constexpr uint32_t F_OFF_SMALL = F_OFF_P + 3 * F_QPANEL;
-constexpr uint32_t T_C = 0, T_A = 128, T_Z = 272;      // TMEM columns: C (128), A (144), Z (128)
-constexpr int EPI_WARPS = 8;
+constexpr uint32_t F_OFF_O = F_OFF_C + F_QTILE;       // q_clean staging (same layout as a Q tile)
+constexpr uint32_t F_OFF_SMALL = F_OFF_O + F_QTILE;
+constexpr uint32_t T_C = 0, T_R = 128, T_RSTRIDE = 144;  // TMEM columns: C, then regions 0 and 1
+constexpr uint32_t T_P = 416;                          // P' (64 + 8 columns of packed pairs)
+constexpr int GROUP_WARPS = 8;
 
 struct FwdSmall {
-  float xchg[2][128];
-  float cf[128];
-  uint64_t full[2], kready[2], empty[2];
-  uint64_t a_full, a_free, c_read, cconv, cprev_free, c_full, pready, z_full, z_free, mma_done;
+  float xs[2][2][128];     // [chunk parity][column half][row]: partial s_t
+  float cf[2][128];        // [chunk parity][row]: lambda_t / pos_t
+  float msum[4][128];      // aux: per token-quarter partial key sums
+  uint64_t full[2], kready[2], empty[2], a_full[2], a_free[2], cf_ready[2], z_full[2], z_free[2];
+  uint64_t c_full, c_read, cprev_free, cconv, pready, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -68,25 +77,6 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
-}
-__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-// 4 consecutive fp32 TMEM columns of this thread's lane
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
-  uint32_t r0, r1, r2, r3;
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(taddr));
-  v[0] = __uint_as_float(r0);
-  v[1] = __uint_as_float(r1);
-  v[2] = __uint_as_float(r2);
-  v[3] = __uint_as_float(r3);
 }
 
 template <int AB16>
@@ -113,18 +103,33 @@ __device__ __forceinline__ uint32_t to16(float x) {
   return (uint32_t)__half_as_ushort(__float2half_rn(x));
 }
 
+// 4 consecutive fp32 TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float* v) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(taddr));
+  v[0] = __uint_as_float(r0);
+  v[1] = __uint_as_float(r1);
+  v[2] = __uint_as_float(r2);
+  v[3] = __uint_as_float(r3);
+}
+
+// 64 values of one row -> one 64-column panel row (8 swizzled 16-byte chunks)
 template <int AB16>
-__device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const float* v) {
+__device__ __forceinline__ void store_row64(uint32_t panel, int row, const float* x) {
 #pragma unroll
   for (int cc = 0; cc < 8; ++cc)
-    st_shared_v4(panel + sw128(row, cc), pack2<AB16>(v[8 * cc], v[8 * cc + 1]), pack2<AB16>(v[8 * cc + 2], v[8 * cc + 3]),
-                 pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]), pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
+    st_shared_v4(panel + sw128(row, cc), pack2<AB16>(x[8 * cc], x[8 * cc + 1]), pack2<AB16>(x[8 * cc + 2], x[8 * cc + 3]),
+                 pack2<AB16>(x[8 * cc + 4], x[8 * cc + 5]), pack2<AB16>(x[8 * cc + 6], x[8 * cc + 7]));
 }
 
 template <int AB16>
 __global__ void __launch_bounds__(F_THREADS, 1)
-    tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk, CleanArgs a,
-                  int* err) {
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                  const __grid_constant__ CUtensorMap tmo, CleanArgs a, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   FwdSmall& S = *reinterpret_cast<FwdSmall*>(sm + F_OFF_SMALL);
@@ -142,17 +147,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.kready[i], 1);
-      mbar_init(&S.empty[i], 2 + EPI_WARPS);
+      mbar_init(&S.empty[i], 2 + GROUP_WARPS);
+      mbar_init(&S.a_full[i], 1);
+      mbar_init(&S.a_free[i], GROUP_WARPS);
+      mbar_init(&S.cf_ready[i], GROUP_WARPS / 2);
+      mbar_init(&S.z_full[i], 1);
+      mbar_init(&S.z_free[i], GROUP_WARPS);
     }
-    mbar_init(&S.a_full, 1);
-    mbar_init(&S.a_free, EPI_WARPS);
-    mbar_init(&S.c_read, EPI_WARPS);
-    mbar_init(&S.cconv, EPI_WARPS);
-    mbar_init(&S.cprev_free, 1);
     mbar_init(&S.c_full, 1);
-    mbar_init(&S.pready, EPI_WARPS);
-    mbar_init(&S.z_full, 1);
-    mbar_init(&S.z_free, EPI_WARPS);
+    mbar_init(&S.c_read, GROUP_WARPS);
+    mbar_init(&S.cprev_free, 1);
+    mbar_init(&S.cconv, GROUP_WARPS);
+    mbar_init(&S.pready, GROUP_WARPS);
     mbar_init(&S.mma_done, 1);
     S.abort = 0;
     fence_barrier_init();
@@ -189,47 +195,71 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // Four MMA groups per chunk i, each issued once its inputs are ready (checked without
+    // blocking, so a group of chunk i+1 can go ahead of a group of chunk i that still waits):
+    //   F1_i  needs K/Q tiles of i and region i%2 free (Z of i-2 read);
+    //   F3_i  needs C of i-1 read out of TMEM;
+    //   F2a_i needs bf16 C_prev in shared memory and the scores A_i read (Z_i overwrites them);
+    //   F2b_i needs P'_i; F2b_i's commit also releases the K/Q stage, so F1_i, F3_i and F2a_i of the
+    //         same chunk are issued before it.
     if (lane == 0) {
       const uint32_t id_a = idesc_f16(128, 144, AB16, 0, 0);
       const uint32_t id_z = idesc_f16(128, 128, AB16, 0, 1);
       const uint32_t id_c = idesc_f16(128, 128, AB16, 1, 1);
-      const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
-      bool ok = true;
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int s = c & 1;
-        const uint32_t sQ = sbase + F_OFF_Q + s * F_QTILE, sK = sbase + F_OFF_K + s * F_KTILE;
-        ok = pipe_wait(&S.kready[s], (c >> 1) & 1, ab, err, 2) && (c == 0 || pipe_wait(&S.a_free, (c - 1) & 1, ab, err, 2));
-        if (!ok) break;
-        tc_fence_after();
+      const uint32_t sC = sbase + F_OFF_C;
+      int i1 = 0, i3 = 0, i2a = 0, i2b = 0;
+      long long idle0 = clock64();
+      while (i2b < nchunks) {
+        if (*ab) break;
+        bool issued = true;
+        if (i2b < i2a && i2b < i3 && mbar_test(&S.pready, i2b & 1)) {
+          const int c = i2b, s = c & 1;
+          const uint32_t sK = sbase + F_OFF_K + s * F_KTILE;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma(tbase + T_A, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
-               sdesc(sK + (ks >> 2) * F_KPANEL + (ks & 3) * 32, 16, 1024), id_a, ks > 0);
-        umma_commit(&S.a_full);
-        ok = pipe_wait(&S.c_read, c & 1, ab, err, 2);
-        if (!ok) break;
-        tc_fence_after();
+          for (int ks = 0; ks < 9; ++ks)
+            umma_ts(tbase + T_R + T_RSTRIDE * s, tbase + T_P + 8 * ks, sdesc(sK + ks * 2048, F_KPANEL, 1024), id_z, 1);
+          umma_commit(&S.z_full[s]);
+          umma_commit(&S.empty[s]);
+          ++i2b;
+        } else if (i2a < i1 && mbar_test(&S.cconv, i2a & 1) && mbar_test(&S.a_free[i2a & 1], (i2a >> 1) & 1)) {
+          const uint32_t sQ = sbase + F_OFF_Q + (i2a & 1) * F_QTILE;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma(tbase + T_C, sdesc(sK + ks * 2048, F_KPANEL, 1024), sdesc(sK + ks * 2048, F_KPANEL, 1024), id_c, 1);
-        umma_commit(&S.c_full);
-        ok = pipe_wait(&S.cconv, c & 1, ab, err, 2) && (c == 0 || pipe_wait(&S.z_free, (c - 1) & 1, ab, err, 2));
-        if (!ok) break;
-        tc_fence_after();
+          for (int ks = 0; ks < 8; ++ks)
+            umma(tbase + T_R + T_RSTRIDE * (i2a & 1), sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
+                 sdesc(sC + ks * 2048, F_QPANEL, 1024), id_z, ks > 0);
+          umma_commit(&S.cprev_free);
+          ++i2a;
+        } else if (i3 < i1 && mbar_test(&S.c_read, i3 & 1)) {
+          const uint32_t sK = sbase + F_OFF_K + (i3 & 1) * F_KTILE;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma(tbase + T_Z, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
-               sdesc(sC + ks * 2048, F_QPANEL, 1024), id_z, ks > 0);
-        umma_commit(&S.cprev_free);
-        ok = pipe_wait(&S.pready, c & 1, ab, err, 2);
-        if (!ok) break;
-        tc_fence_after();
+          for (int ks = 0; ks < 8; ++ks)
+            umma(tbase + T_C, sdesc(sK + ks * 2048, F_KPANEL, 1024), sdesc(sK + ks * 2048, F_KPANEL, 1024), id_c, 1);
+          umma_commit(&S.c_full);
+          ++i3;
+        } else if (i1 < nchunks && mbar_test(&S.kready[i1 & 1], (i1 >> 1) & 1) &&
+                   (i1 < 2 || mbar_test(&S.z_free[i1 & 1], ((i1 - 2) >> 1) & 1))) {
+          const int b = i1 & 1;
+          const uint32_t sQ = sbase + F_OFF_Q + b * F_QTILE, sK = sbase + F_OFF_K + b * F_KTILE;
+          tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 9; ++ks)
-          umma(tbase + T_Z, sdesc(sP + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
-               sdesc(sK + ks * 2048, F_KPANEL, 1024), id_z, 1);
-        umma_commit(&S.z_full);
-        umma_commit(&S.empty[s]);
+          for (int ks = 0; ks < 8; ++ks)
+            umma(tbase + T_R + T_RSTRIDE * b, sdesc(sQ + (ks >> 2) * F_QPANEL + (ks & 3) * 32, 16, 1024),
+                 sdesc(sK + (ks >> 2) * F_KPANEL + (ks & 3) * 32, 16, 1024), id_a, ks > 0);
+          umma_commit(&S.a_full[b]);
+          ++i1;
+        } else {
+          issued = false;
+        }
+        if (issued) {
+          idle0 = clock64();
+        } else if (clock64() - idle0 > (1ll << 31)) {
+          *ab = 1;
+          atomicOr(err, 2);
+          break;
+        }
       }
       // TMEM is freed only after every issued MMA has completed
       umma_commit(&S.mma_done);
@@ -237,10 +267,13 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     }
   } else if (warp < 4) {
     // ------------------------------------------------------------------ aux: running key sum
-    const int at = threadIdx.x - 64;           // 0..63, owns dims 2at, 2at+1
-    const uint32_t p = at >> 5;                // panel
-    const uint32_t e = (2 * at) & 63;          // element inside the panel row
+    const int at = threadIdx.x - 64;           // 0..63
+    // m rows: this thread writes dims 2at, 2at+1
+    const uint32_t p = at >> 5;
+    const uint32_t e = (2 * at) & 63;
     const uint32_t ch = e >> 3, cb = (e & 7) * 2;
+    // key sums: this thread adds 16-byte chunk cq (dims 8cq..8cq+7) over tokens 32tq..32tq+31
+    const int cq = at & 15, tq = at >> 4;
     float m0v = 0.f, m1v = 0.f;
     if (sub_mean && a.initial_mean) {
       m0v = a.initial_mean[st_base + 2 * at];
@@ -280,16 +313,24 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       nbar_sync(2, 64);
       if (at == 0) mbar_arrive(&S.kready[s]);
       if (sub_mean) {
-        float acc0 = 0.f, acc1 = 0.f;
-        const uint32_t kb = kt + p * F_KPANEL + cb;
-#pragma unroll 8
-        for (int tt = 0; tt < F_BT; ++tt) {
-          const float2 f = unpack2<AB16>(ld_shared_u32(kb + sw128(tt, ch)));
-          acc0 += f.x;
-          acc1 += f.y;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const uint32_t kb = kt + (cq >> 3) * F_KPANEL;
+#pragma unroll 4
+        for (int tt = 32 * tq; tt < 32 * tq + 32; ++tt) {
+          const uint4 v4 = ld_shared_v4(kb + sw128(tt, cq & 7));
+          const uint32_t w4[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack2<AB16>(w4[i]);
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          }
         }
-        m0v += acc0;
-        m1v += acc1;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) S.msum[tq][8 * cq + i] = acc[i];
+        nbar_sync(2, 64);
+        m0v += S.msum[0][2 * at] + S.msum[1][2 * at] + S.msum[2][2 * at] + S.msum[3][2 * at];
+        m1v += S.msum[0][2 * at + 1] + S.msum[1][2 * at + 1] + S.msum[2][2 * at + 1] + S.msum[3][2 * at + 1];
       }
       nbar_sync(2, 64);
       if (at == 0) mbar_arrive(&S.empty[s]);
@@ -298,23 +339,95 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       a.final_mean[st_base + 2 * at] = m0v;
       a.final_mean[st_base + 2 * at + 1] = m1v;
     }
-  } else {
-    // ------------------------------------------------------------------ epilogue (256 threads)
-    const int et = threadIdx.x - 128;
-    const int g = et >> 7;                        // column half
+  } else if (warp < 4 + GROUP_WARPS) {
+    // ------------------------------------------------------------------ score group: A -> P'
     const int qd = warp & 3;                      // TMEM lane quadrant of this warp
-    const int r = 32 * qd + lane;                 // token (A, Z) or state row (C)
-    const int pair = 3 + qd;                      // named barrier shared by warps qd+4 and qd+8
+    const int hp = (warp - 4) >> 2;               // column half: columns 64hp .. 64hp+63
+    const int t = 32 * qd + lane;                 // token of this thread
     const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
-    const uint32_t sC = sbase + F_OFF_C, sP = sbase + F_OFF_P;
     const float gate_b = gate ? a.gate_b[h] : 0.f;
-    // diagonal relation of this warp's 32 rows with this half's 64 columns
-    const bool cols_all_below = 64 * g + 63 < 32 * qd;    // every column j < every row t
-    const bool cols_all_above = 64 * g > 32 * qd + 31;    // every column j > every row t
+    const bool cols_below = 64 * hp + 63 < 32 * qd;
+    const bool cols_above = 64 * hp > 32 * qd + 31;
     float v[64];
+    // P' entries above the diagonal block never change: zero them once; so do mean columns 2..15
+    {
+      const uint32_t z8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      if (cols_above)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tmem_st8(lrow + T_P + 32 * hp + 8 * i, z8);
+      if (hp == 0) tmem_st8(lrow + T_P + 64, z8);
+      tmem_st_wait();
+    }
+
+    for (int c = 0; c < nchunks; ++c) {
+      const int pb = c & 1;
+      const int t0 = c * F_BT;
+      const int valid = min(F_BT, sq.len - t0);
+      pipe_wait(&S.a_full[pb], (c >> 1) & 1, ab, err, 16);
+      tc_fence_after();
+      float ext[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!cols_above) tmem_ld64(lrow + T_R + T_RSTRIDE * pb + 64 * hp, v);
+      if (hp == 0) tmem_ld4(lrow + T_R + T_RSTRIDE * pb + 128, ext);
+      tc_fence_before();
+      warp_arrive(&S.a_free[pb]);
+      const float ipos = 1.f / position_of(t0 + t, a.position_offset);
+      float part = ext[0] + ext[1];
+      if (!cols_above) {
+        if (!cols_below) {
+#pragma unroll
+          for (int jj = 0; jj < 64; ++jj) v[jj] = (64 * hp + jj <= t) ? v[jj] : 0.f;
+        }
+        float tr[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tr[i] = (v[i] + v[i + 16]) + (v[i + 32] + v[i + 48]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tr[i] = (tr[i] + tr[i + 4]) + (tr[i + 8] + tr[i + 12]);
+        part += (tr[0] + tr[1]) + (tr[2] + tr[3]);
+      }
+      S.xs[pb][hp][t] = part;
+      nbar_sync(3 + qd, 64);
+      const float st = sub_mean ? S.xs[pb][0][t] + S.xs[pb][1][t] : 0.f;
+      const float sp = st * ipos;
+      if (hp == 0) {
+        float lamv;
+        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
+        else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
+        S.cf[pb][t] = lamv * ipos;
+        if (a.token_aux && t < valid) {
+          float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
+          *aux = make_float2(lamv, st);
+        }
+        warp_arrive(&S.cf_ready[pb]);
+      }
+      // the P' buffer is free once F2b of the previous chunk has completed
+      if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 16);
+      if (!cols_above) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {  // packed in place: v[i] <- (v[2i], v[2i+1])
+          const float lo = (cols_below || 64 * hp + 2 * i <= t) ? v[2 * i] - sp : 0.f;
+          const float hi = (cols_below || 64 * hp + 2 * i + 1 <= t) ? v[2 * i + 1] - sp : 0.f;
+          v[i] = __uint_as_float(pack2<AB16>(lo, hi));
+        }
+        tmem_st32(lrow + T_P + 32 * hp, v);
+      }
+      if (hp == 0) tmem_st1(lrow + T_P + 64, pack2<AB16>(-sp, -sp));
+      tmem_st_wait();
+      tc_fence_before();
+      warp_arrive(&S.pready);
+    }
+  } else {
+    // ------------------------------------------------------------------ output group: C, q_clean
+    const int qd = warp & 3;
+    const int ho = (warp - 4 - GROUP_WARPS) >> 2;  // column half: columns 64ho .. 64ho+63
+    const int r = 32 * qd + lane;                  // state row (C) or token (Z)
+    const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
+    const uint32_t cpan = sbase + F_OFF_C + (uint32_t)ho * F_QPANEL;
+    const bool leader = warp == 4 + GROUP_WARPS && lane == 0;  // issues the bulk stores
+    float v[64];
+
     // initial state -> TMEM C and the bf16 operand for chunk 0
     if (a.initial_cov) {
-      const float4* src = reinterpret_cast<const float4*>(a.initial_cov + (st_base + r) * 128 + 64 * g);
+      const float4* src = reinterpret_cast<const float4*>(a.initial_cov + (st_base + r) * 128 + 64 * ho);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float4 f = src[i];
@@ -324,16 +437,14 @@ __global__ void __launch_bounds__(F_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) v[i] = 0.f;
     }
-    tmem_st32(lrow + T_C + 64 * g, v);
-    tmem_st32(lrow + T_C + 64 * g + 32, v + 32);
+    tmem_st32(lrow + T_C + 64 * ho, v);
+    tmem_st32(lrow + T_C + 64 * ho + 32, v + 32);
     if (nchunks == 0 && a.final_cov) {
-      float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * g);
+      float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * ho);
 #pragma unroll
       for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
-    store_panel_row<AB16>(sC + g * F_QPANEL, r, v);
-    // constant part of the mean columns of P' (columns 136..143 stay zero)
-    st_shared_v4(sP + 2 * F_QPANEL + sw128(r, 1 + g), 0u, 0u, 0u, 0u);
+    store_row64<AB16>(cpan, r, v);
     tmem_st_wait();
     fence_async_smem();
     tc_fence_before();
@@ -344,99 +455,66 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       const int s = c & 1;
       const int t0 = c * F_BT;
       const int valid = min(F_BT, sq.len - t0);
-      const int t = r;
-      // ---------------- P' = (A - s/pos) on and below the diagonal, plus the mean columns
-      pipe_wait(&S.a_full, c & 1, ab, err, 16);
-      tc_fence_after();
-      tmem_ld64(lrow + T_A + 64 * g, v);
-      float ext[4] = {0.f, 0.f, 0.f, 0.f};
-      if (g == 0) tmem_ld4(lrow + T_A + 128, ext);
-      tc_fence_before();
-      warp_arrive(&S.a_free);
-      const float ipos = 1.f / position_of(t0 + t, a.position_offset);
-      float part = 0.f;
-      if (cols_all_below) {
-#pragma unroll
-        for (int jj = 0; jj < 64; ++jj) part += v[jj];
-      } else if (!cols_all_above) {
-#pragma unroll
-        for (int jj = 0; jj < 64; ++jj) part += (64 * g + jj <= t) ? v[jj] : 0.f;
-      }
-      float lamv = 0.f;
-      if (g == 0) {
-        part += ext[0] + ext[1];
-        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
-        else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
-        S.cf[t] = lamv * ipos;
-      }
-      // pair exchange of the partial row sums (warps qd+4 and qd+8 hold the same rows)
-      S.xchg[g][t] = part;
-      nbar_sync(pair, 64);
-      {
-        const float st = sub_mean ? S.xchg[0][t] + S.xchg[1][t] : 0.f;
-        const float sp = st * ipos;
-        if (g == 0 && a.token_aux && t < valid) {
-          float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
-          *aux = make_float2(lamv, st);
-        }
-        if (cols_all_above) {
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) st_shared_v4(sP + g * F_QPANEL + sw128(t, cc), 0u, 0u, 0u, 0u);
-        } else if (cols_all_below) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] -= sp;
-          store_panel_row<AB16>(sP + g * F_QPANEL, t, v);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = (64 * g + i <= t) ? v[i] - sp : 0.f;
-          store_panel_row<AB16>(sP + g * F_QPANEL, t, v);
-        }
-        if (g == 0) {
-          const uint32_t nsp = pack2<AB16>(-sp, -sp);
-          st_shared_v4(sP + 2 * F_QPANEL + sw128(t, 0), nsp, 0u, 0u, 0u);
-        }
-      }
-      fence_async_smem();
-      warp_arrive(&S.pready);
-      // ---------------- C after this chunk -> bf16 operand of the next chunk (or the final state)
+      // ---------------- C after chunk c -> bf16 operand of chunk c+1 (or the final state)
       pipe_wait(&S.c_full, c & 1, ab, err, 32);
       tc_fence_after();
-      tmem_ld64(lrow + T_C + 64 * g, v);
+      tmem_ld64(lrow + T_C + 64 * ho, v);
       tc_fence_before();
       warp_arrive(&S.c_read);
       if (c + 1 < nchunks) {
         pipe_wait(&S.cprev_free, c & 1, ab, err, 64);
-        store_panel_row<AB16>(sC + g * F_QPANEL, r, v);
+        store_row64<AB16>(cpan, r, v);
         fence_async_smem();
       } else if (a.final_cov) {
-        float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * g);
+        float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * ho);
 #pragma unroll
         for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
       warp_arrive(&S.cconv);
-      // ---------------- q_clean = q - (lambda / pos) Z
-      pipe_wait(&S.z_full, c & 1, ab, err, 128);
+      // ---------------- q_clean of chunk c = q - (lambda / pos) Z
+      pipe_wait(&S.z_full[s], (c >> 1) & 1, ab, err, 128);
       tc_fence_after();
-      tmem_ld64(lrow + T_Z + 64 * g, v);
+      tmem_ld64(lrow + T_R + T_RSTRIDE * s + 64 * ho, v);
       tc_fence_before();
-      warp_arrive(&S.z_free);
-      {
-        const float cf = S.cf[t];
-        const uint32_t qrow = sbase + F_OFF_Q + s * F_QTILE + g * F_QPANEL;
-        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.q_clean + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
+      warp_arrive(&S.z_free[s]);
+      pipe_wait(&S.cf_ready[s], (c >> 1) & 1, ab, err, 128);
+      const float cf = S.cf[s][r];
+      const uint32_t qpan = sbase + F_OFF_Q + s * F_QTILE + (uint32_t)ho * F_QPANEL;
+      const uint32_t opan = sbase + F_OFF_O + (uint32_t)ho * F_QPANEL;
+      // the staging tile is free once the previous bulk store has read it
+      if (leader) bulk_wait_read();
+      nbar_sync(7, 32 * GROUP_WARPS);
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint4 qv = ld_shared_v4(qrow + sw128(t, cc));
-          const uint4 o = make_uint4(sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
-                                     sub2<AB16>(qv.y, pack2<AB16>(cf * v[8 * cc + 2], cf * v[8 * cc + 3])),
-                                     sub2<AB16>(qv.z, pack2<AB16>(cf * v[8 * cc + 4], cf * v[8 * cc + 5])),
-                                     sub2<AB16>(qv.w, pack2<AB16>(cf * v[8 * cc + 6], cf * v[8 * cc + 7])));
-          if (t < valid) orow[cc] = o;
+      for (int cc = 0; cc < 8; ++cc) {
+        const uint4 qv = ld_shared_v4(qpan + sw128(r, cc));
+        st_shared_v4(opan + sw128(r, cc), sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
+                     sub2<AB16>(qv.y, pack2<AB16>(cf * v[8 * cc + 2], cf * v[8 * cc + 3])),
+                     sub2<AB16>(qv.z, pack2<AB16>(cf * v[8 * cc + 4], cf * v[8 * cc + 5])),
+                     sub2<AB16>(qv.w, pack2<AB16>(cf * v[8 * cc + 6], cf * v[8 * cc + 7])));
+      }
+      warp_arrive(&S.empty[s]);  // q of this chunk has been read
+      if (valid == F_BT) {
+        fence_async_smem();
+        nbar_sync(7, 32 * GROUP_WARPS);
+        if (leader) {
+          const int row = (int)(sq.bos + (int64_t)t0);
+          tma_store_3d(&tmo, sm + F_OFF_O, 0, h, row);
+          tma_store_3d(&tmo, sm + F_OFF_O + F_QPANEL, 64, h, row);
+          bulk_commit();
+        }
+      } else {
+        // partial chunk: this warp's 32 rows x 64 columns, four 128-byte row segments per store
+        __syncwarp();
+        uint8_t* obase = (uint8_t*)a.q_clean + ((sq.bos + t0) * H + h) * 256 + ho * 128 + (lane & 7) * 16;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = 32 * qd + 4 * i + (lane >> 3);
+          const uint4 ov = ld_shared_v4(opan + sw128(row, lane & 7));
+          if (row < valid) *reinterpret_cast<uint4*>(obase + (int64_t)row * H * 256) = ov;
         }
       }
-      nbar_sync(pair, 64);  // both halves have read S.cf before the next chunk rewrites it
-      warp_arrive(&S.empty[s]);
     }
+    if (leader) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -448,17 +526,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
 
 template <int AB16>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  CUtensorMap tq, tk;
+  CUtensorMap tq, tk, to;
   const int64_t rows = (int64_t)a.B * a.T;
   cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, F_BT, AB16 != 0);
   if (e != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&to, a.q_clean, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
   int* err = reinterpret_cast<int*>(a.workspace);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
   auto kern = tc_fwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, a, err);
+  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, to, a, err);
   *launches += 1;
   return cudaGetLastError();
 }
