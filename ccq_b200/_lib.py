@@ -19,7 +19,7 @@ CCQ_OP_FWD, CCQ_OP_BWD, CCQ_OP_DECODE = 0, 1, 2
 PATHS = {0: 'none', 1: 'simt', 2: 'tcgen05', 3: 'decode'}
 
 EXPORTS = ('ccq_last_error', 'ccq_last_path', 'ccq_version', 'ccq_last_launch_count',
-           'ccq_workspace_size', 'ccq_clean_fwd', 'ccq_clean_bwd', 'ccq_decode_step')
+           'ccq_workspace_size', 'ccq_clean_fwd', 'ccq_clean_bwd', 'ccq_decode_step', 'ccq_clean_bwd_noalloc')
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -35,6 +35,8 @@ _SIGS = {
                            _P, _SZ, _P]),
     'ccq_clean_bwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P,
                            _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    'ccq_clean_bwd_noalloc': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     'ccq_decode_step': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
 }
 

@@ -1,6 +1,7 @@
 // C ABI of the B200 CCQ cleaning operator: argument validation, dispatch and error reporting.
 // Declarations and contracts: include/ccq_b200.h.
 #include <stdarg.h>
+#include <mutex>
 #include <stdio.h>
 #include <string.h>
 
@@ -208,3 +209,64 @@ int ccq_decode_step(int dtype, int B, int T, int H, int K, const void* q, const 
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Backward without allocation: the scratch is a fixed device array of this library, looked up once
+// per device with that device current.  The existing ccq_clean_bwd does the validation, dispatch and
+// launches; this wrapper only supplies the scratch.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CCQ_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoallocMaxDevices = 64;
+void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(CCQ_ERR_UNSUPPORTED, "ccq_clean_bwd_noalloc: device %d, supported are devices 0..%d", dev,
+                kNoallocMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd_noalloc: cudaGetSymbolAddress of the scratch");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CCQ_OK;
+}
+
+}  // namespace
+
+extern "C" int ccq_clean_bwd_noalloc(int dtype, int B, int T, int H, int K, const void* q, const void* k,
+                                     int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                                     const int64_t* cu_seqlens, int n_seqs, int position_offset, int subtract_mean,
+                                     const float* initial_cov, const float* initial_mean, const float* state_cov,
+                                     const float* state_mean, const float* token_aux, const void* dq_clean,
+                                     const float* dfinal_cov, const float* dfinal_mean, void* dq, void* dk,
+                                     float* dlam, float* dgate_w, float* dgate_b, float* dinitial_cov,
+                                     float* dinitial_mean, void* stream) {
+  g_err[0] = 0;
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st != CCQ_OK) return st;
+  st = ccq_clean_bwd(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs, position_offset,
+                     subtract_mean, initial_cov, initial_mean, state_cov, state_mean, token_aux, dq_clean, dfinal_cov,
+                     dfinal_mean, dq, dk, dlam, dgate_w, dgate_b, dinitial_cov, dinitial_mean, scratch,
+                     CCQ_NOALLOC_SCRATCH_BYTES, stream);
+  if (st == CCQ_ERR_WORKSPACE) {
+    char detail[512];
+    snprintf(detail, sizeof(detail), "%s", g_err);
+    return fail(CCQ_ERR_WORKSPACE,
+                "ccq_clean_bwd_noalloc: the call needs more scratch than the fixed %u bytes (%s); "
+                "use ccq_clean_bwd with a workspace",
+                (unsigned)CCQ_NOALLOC_SCRATCH_BYTES, detail);
+  }
+  return st;
+}
+

@@ -114,6 +114,38 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K,
                   void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Backward that allocates nothing.  No counterpart in the reference: the reference's backward gets
+ * its scratch from PyTorch's allocator.  This entry point is for callers that cannot hand over a
+ * device workspace, for instance a host binding without a device allocator of its own, or a
+ * serving loop that keeps the allocator out of its steady state.
+ *
+ * Same arguments, outputs and errors as ccq_clean_bwd, minus workspace / workspace_bytes: the
+ * scratch is a fixed array of CCQ_NOALLOC_SCRATCH_BYTES (1 MiB) in the library's device data.
+ *   - A call whose scratch need, on the path it takes, exceeds 1 MiB fails with CCQ_ERR_WORKSPACE
+ *     before anything is launched.  The tensor-core backward (bf16 / fp16, K = 128) needs
+ *     256 + 516 * n_seqs * H bytes, so it fits up to n_seqs * H = 2031; the exact fp32 backward's
+ *     need grows with the sequence length (ccq_workspace_size bounds both paths from above).
+ *   - The first call on each device looks the scratch up (cudaGetSymbolAddress, with that device
+ *     current) and may load the library's device code; make that first call before any stream
+ *     capture begins.
+ *   - All calls on one device share the one scratch array: calls that overlap in time (other
+ *     streams, other host threads) race and give wrong results.  Calls issued one after the other
+ *     on one stream are safe.
+ *   - The kernels clear the part of the scratch that must start at zero on every call.
+ */
+#define CCQ_NOALLOC_SCRATCH_BYTES (1u << 20)
+int ccq_clean_bwd_noalloc(int dtype, int B, int T, int H, int K,
+                          const void* q, const void* k,
+                          int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                          const int64_t* cu_seqlens, int n_seqs,
+                          int position_offset, int subtract_mean,
+                          const float* initial_cov, const float* initial_mean,
+                          const float* state_cov, const float* state_mean, const float* token_aux,
+                          const void* dq_clean, const float* dfinal_cov, const float* dfinal_mean,
+                          void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
+                          float* dinitial_cov, float* dinitial_mean, void* stream);
+
+/*
  * Recurrent (decode / short prefill) cleaning with the generation cache.
  * Replaces fla fused_recurrent_gla(q, k, v=k, scale=1) + _CCQCleanQ as called by
  * fused_ccq_clean(use_chunk=False) (ccq/ops/ccq_gdn/fused_clean.py:34-83) and
