@@ -31,6 +31,9 @@ sys.path.insert(0, ROOT)
 FWD_BYTES_PER_TH = 768      # q, k read + q_clean write (bf16)
 BWD_BYTES_PER_TH = 1280     # q, k, dq_clean read + dq, dk write (bf16)
 FLOP_PER_TH = 339968
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
+# kernel at c2; profiles/tc_fwd_kernel_c2.md and profiles/tc_bwd_kernel_c2.md give the command.
+NCU_TRAFFIC_C2 = {'fwd': 269.0e6 + 110.8e6, 'bwd': 415.5e6 + 231.6e6}
 DECODE_BYTES_PER_TH = 2 * 128 * 128 * 4 + 2 * 128 * 4 + 4 * 128 * 2 + 2 * 2
 
 
@@ -323,7 +326,8 @@ def run_ours(args, rank, world, local_rank):
                        'l2': 'inputs larger than L2 (q,k,dq_clean 384 MiB per GPU)',
                        'paths': {'fwd': path_fwd, 'bwd': path_bwd}},
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s',
-                         'frac': achieved / hbm_peak, 'traffic': None,
+                         'frac': achieved / hbm_peak, 'traffic': NCU_TRAFFIC_C2['bwd' if dom_bwd else 'fwd'],
+                         'traffic_unit': 'bytes per launch (ncu)',
                          'kernel': 'bwd' if dom_bwd else 'fwd', 'peak_kind': peak_kind,
                          'op_roofline_frac': roof_time / (elapsed / args.steps / 1),
                          'fwd_ms': t_fwd * 1e3, 'bwd_ms': t_bwd * 1e3},
