@@ -18,8 +18,9 @@
 // These are the reference's gradients (ccq/ops/common/fused_read.py:18-25, kernel :177-307,
 // carry :355-376, dC0 / dm0 :420-450).
 //
-// Warp roles (384 threads): warp 0 TMA, warp 1 TMEM + MMA issue, warps 2-3 aux (partial-chunk
-// key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.
+// Warp roles (384 threads): warp 0 TMA (it also writes each chunk's dk, staged by the epilogue in
+// the stage's K tile, with a bulk store before reloading the stage), warp 1 TMEM + MMA issue, warps
+// 2-3 aux (partial-chunk key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.
 #include "args.h"
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -126,7 +127,8 @@ __device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const f
 template <int AB16>
 __global__ void __launch_bounds__(B_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmg, CleanArgs a, int* err, float* gate_part) {
+                  const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdq,
+                  const __grid_constant__ CUtensorMap tmdk, CleanArgs a, int* err, float* gate_part) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwdSmall& S = *reinterpret_cast<BwdSmall*>(sm + B_OFF_SMALL);
@@ -166,14 +168,31 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (chunks in reverse)
+    // A stage is reloaded once every reader released it; by then the epilogue has staged that chunk's
+    // dk in the stage's K tile, and this thread writes it out first (full chunks only).
     if (lane == 0) {
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmg);
+      tma_prefetch_desc(&tmdk);
+      auto store_dk = [&](int j) {
+        const int cj = nchunks - 1 - j;
+        if (sq.len - cj * B_BT >= B_BT) {
+          const int row = (int)(sq.bos + (int64_t)cj * B_BT);
+          uint8_t* kt = sm + (j & 1) * B_STAGE + B_OFF_K;
+          tma_store_3d(&tmdk, kt, 0, h, row);
+          tma_store_3d(&tmdk, kt + B_KPANEL, 64, h, row);
+          bulk_commit();
+          bulk_wait_read();
+        }
+      };
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
         const int s = i & 1, c = nchunks - 1 - i;
-        if (i >= 2 && !pipe_wait(&S.empty[s], ((i - 2) >> 1) & 1, ab, err, 1)) break;
+        if (i >= 2) {
+          if (!pipe_wait(&S.empty[s], ((i - 2) >> 1) & 1, ab, err, 1)) break;
+          store_dk(i - 2);
+        }
         if (*ab) break;
         mbar_arrive_expect_tx(&S.full[s], 6 * 8192);
         const int row = (int)(sq.bos + (int64_t)c * B_BT);
@@ -187,6 +206,11 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         ++issued;
       }
       for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i) mbar_wait(&S.full[i & 1], (i >> 1) & 1);
+      if (issued == nchunks) {  // the last one or two chunks: write their dk once released
+        for (int i = (nchunks > 2 ? nchunks - 2 : 0); i < nchunks; ++i)
+          if (pipe_wait(&S.empty[i & 1], (i >> 1) & 1, ab, err, 1)) store_dk(i);
+      }
+      bulk_wait_all();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -394,6 +418,9 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const int valid = min(B_BT, sq.len - t0);
       const uint32_t st = sbase + s * B_STAGE;
       const bool tv = t < valid;
+      // this token's (lambda, s) from the forward, loaded early so its latency hides behind E0G
+      float2 ax = make_float2(0.f, 0.f);
+      if (tv) ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
       // ---------------- G (after this chunk) -> bf16 operand of B3
       if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
       tc_fence_after();
@@ -408,33 +435,41 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);
       if (i >= 1) pipe_wait(&S.cw_done, (i - 1) & 1, ab, err, 32);
       tc_fence_after();
-      float lamv = 0.f, sv = 0.f;
-      if (tv) {
-        const float2 ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
-        lamv = ax.x;
-        sv = sub_mean ? ax.y : 0.f;
-      }
+      const float lamv = ax.x, sv = sub_mean ? ax.y : 0.f;
       const float ipos = 1.f / position_of(t0 + t, a.position_offset);
       const float alpha = lamv * ipos;
       tmem_ld32(lrow + T_DA + 32 * g, v);
       const float* mp = S.m_buf[s];
       if (dside) {
         float wp = 0.f;
-        if (cols_below) {
+        if (!cols_above) {
+          float tr[8];
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) wp += v[jj];
-        } else if (!cols_above) {
+          for (int k8 = 0; k8 < 8; ++k8) {
+            float x = 0.f;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) wp += (32 * g + jj <= t) ? v[jj] : 0.f;
+            for (int u = 0; u < 4; ++u) {
+              const int jj = 8 * u + k8;
+              x += (cols_below || 32 * g + jj <= t) ? v[jj] : 0.f;
+            }
+            tr[k8] = x;
+          }
+          wp = ((tr[0] + tr[1]) + (tr[2] + tr[3])) + ((tr[4] + tr[5]) + (tr[6] + tr[7]));
         }
         if (sub_mean) {
+          const float4* mp4 = reinterpret_cast<const float4*>(mp + 64 * g);
+          float wq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
             float f[8];
             ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
-#pragma unroll
-            for (int e2 = 0; e2 < 8; ++e2) wp = fmaf(mp[64 * g + 8 * cc + e2], f[e2], wp);
+            const float4 ma = mp4[2 * cc], mb = mp4[2 * cc + 1];
+            wq[0] = fmaf(ma.x, f[0], fmaf(mb.x, f[4], wq[0]));
+            wq[1] = fmaf(ma.y, f[1], fmaf(mb.y, f[5], wq[1]));
+            wq[2] = fmaf(ma.z, f[2], fmaf(mb.z, f[6], wq[2]));
+            wq[3] = fmaf(ma.w, f[3], fmaf(mb.w, f[7], wq[3]));
           }
+          wp += (wq[0] + wq[1]) + (wq[2] + wq[3]);
         }
         S.wpart[g][t] = wp;
         nbar_sync(pair, 64);
@@ -493,6 +528,8 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tc_fence_before();
       warp_arrive(&S.c_read);
       if (i >= 1) pipe_wait(&S.cprev_free, (i - 1) & 1, ab, err, 64);
+      if (et == 0) bulk_wait_read();  // the previous chunk's dq bulk store has read sC
+      nbar_sync(1, 256);
       store_panel_row<AB16>(sC + g * 16384, r, v);
       fence_async_smem();
       warp_arrive(&S.cconv);
@@ -504,14 +541,15 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tc_fence_before();
       warp_arrive(&S.zq_free);
       if (dside) {
-        float up = 0.f;
+        float uq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           float f[8];
           ld_row8<AB16>(st + g * B_QDPANEL, t, cc, f);
 #pragma unroll
-          for (int e2 = 0; e2 < 8; ++e2) up = fmaf(f[e2], v[8 * cc + e2], up);
+          for (int e2 = 0; e2 < 8; ++e2) uq[e2 & 3] = fmaf(f[e2], v[8 * cc + e2], uq[e2 & 3]);
         }
+        const float up = (uq[0] + uq[1]) + (uq[2] + uq[3]);
         S.upart[g][t] = up;
         nbar_sync(pair, 64);
         if (g == 0) {
@@ -531,27 +569,43 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         const float ds = S.ds[t];
         const float dp = gate ? S.dpre[t] : 0.f;
         uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
+        const float4* mp4 = reinterpret_cast<const float4*>(mp + 64 * g);
+        const float4* wh4 = reinterpret_cast<const float4*>(S.wh + 64 * g);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
           const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
+          const float4 ma = mp4[2 * cc], mb = mp4[2 * cc + 1];
+          const float mv[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+          float wv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (gate) {
+            const float4 wa = wh4[2 * cc], wb = wh4[2 * cc + 1];
+            wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
+            wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
+          }
           uint32_t o[4];
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
-            const int jj = 8 * cc + 2 * e2, d0 = 64 * g + jj;
-            float x0 = fmaf(ds, mp[d0], v[jj]);
-            float x1 = fmaf(ds, mp[d0 + 1], v[jj + 1]);
-            if (gate) {
-              x0 = fmaf(dp, S.wh[d0], x0);
-              x1 = fmaf(dp, S.wh[d0 + 1], x1);
-            }
+            const int jj = 8 * cc + 2 * e2;
+            const float x0 = fmaf(dp, wv[2 * e2], fmaf(ds, mv[2 * e2], v[jj]));
+            const float x1 = fmaf(dp, wv[2 * e2 + 1], fmaf(ds, mv[2 * e2 + 1], v[jj + 1]));
             const float2 f = unpack2<AB16>(dw[e2]);
             o[e2] = pack2<AB16>(f.x + x0, f.y + x1);
           }
-          if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+          if (valid == B_BT) st_shared_v4(sC + g * 8192 + sw128(t, cc), o[0], o[1], o[2], o[3]);  // staged
+          else if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       fence_async_smem();
+      if (valid == B_BT) {  // dq of the chunk is staged in sC (B2 has read C_prev): one bulk store
+        nbar_sync(1, 256);
+        if (et == 0) {
+          const int row = (int)(sq.bos + (int64_t)t0);
+          tma_store_3d(&tmdq, sm + B_OFF_C, 0, h, row);
+          tma_store_3d(&tmdq, sm + B_OFF_C + 8192, 64, h, row);
+          bulk_commit();
+        }
+      }
       warp_arrive(&S.dpre_ready);
       warp_arrive(&S.m_free[s]);
 
@@ -569,19 +623,22 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + cwv[0]));
       }
-      nbar_sync(1, 256);
+      if (valid < B_BT) {  // a document's last, partial chunk: plain stores of its valid rows
+        nbar_sync(1, 256);
 #pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        const int qid = et + 256 * k4;             // 16-byte chunk id: row (64) x panel (2) x chunk (8)
-        const int row = qid >> 4, pn = (qid >> 3) & 1, cc = qid & 7;
-        if (row < valid) {
-          const uint4 val = ld_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, cc));
-          *reinterpret_cast<uint4*>((uint8_t*)a.dk + (((sq.bos + t0 + row) * H + h) * 128 + 64 * pn + 8 * cc) * 2) = val;
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int qid = et + 256 * k4;             // 16-byte chunk id: row (64) x panel (2) x chunk (8)
+          const int row = qid >> 4, pn = (qid >> 3) & 1, cc = qid & 7;
+          if (row < valid) {
+            const uint4 val = ld_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, cc));
+            *reinterpret_cast<uint4*>((uint8_t*)a.dk + (((sq.bos + t0 + row) * H + h) * 128 + 64 * pn + 8 * cc) * 2) = val;
+          }
         }
       }
-      fence_async_smem();
+      fence_async_smem();  // the staged dk is read by the TMA thread's bulk store
       warp_arrive(&S.empty[s]);
     }
+    if (et == 0) bulk_wait_all();
     // ---------------- per-document outputs
     if (nchunks > 0) {
       pipe_wait(&S.g_full, (nchunks - 1) & 1, ab, err, 512);
@@ -634,13 +691,16 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
   if (e != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tg, a.dq_clean, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
+  CUtensorMap tdq, tdk;
+  if ((e = tc::make_token_map(&tdq, a.dq, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&tdk, a.dk, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   int* err = reinterpret_cast<int*>(a.workspace);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
   auto kern = tc_bwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, a, err, part);
+  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, a, err, part);
   *launches += 1;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.lambda_mode == LAMBDA_GATE) {

@@ -255,7 +255,10 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         }
         if (issued) {
           idle0 = clock64();
-        } else if (clock64() - idle0 > (1ll << 31)) {
+        } else {
+          __nanosleep(32);  // back off: the polling thread shares its scheduler with epilogue warps
+        }
+        if (!issued && clock64() - idle0 > (1ll << 31)) {
           *ab = 1;
           atomicOr(err, 2);
           break;
