@@ -564,19 +564,30 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           db_acc += dp;
         }
       }
-      if (gate) nbar_sync(tgrp, 128);  // dpre of these tokens is in S.dpre
-      if (!dside) {
+      if (!dside) {  // dq_t = dqc_t + ds_t m_prev + [dq]_t, before dpre is known
         const float ds = S.ds[t];
-        const float dp = gate ? S.dpre[t] : 0.f;
-        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
         const float4* mp4 = reinterpret_cast<const float4*>(mp + 64 * g);
-        const float4* wh4 = reinterpret_cast<const float4*>(S.wh + 64 * g);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
           const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
           const float4 ma = mp4[2 * cc], mb = mp4[2 * cc + 1];
           const float mv[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const float2 f = unpack2<AB16>(dw[e2]);
+            v[8 * cc + 2 * e2] = f.x + fmaf(ds, mv[2 * e2], v[8 * cc + 2 * e2]);
+            v[8 * cc + 2 * e2 + 1] = f.y + fmaf(ds, mv[2 * e2 + 1], v[8 * cc + 2 * e2 + 1]);
+          }
+        }
+      }
+      if (gate) nbar_sync(tgrp, 128);  // dpre of these tokens is in S.dpre
+      if (!dside) {  // + dpre_t W_h, then out
+        const float dp = gate ? S.dpre[t] : 0.f;
+        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
+        const float4* wh4 = reinterpret_cast<const float4*>(S.wh + 64 * g);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
           float wv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           if (gate) {
             const float4 wa = wh4[2 * cc], wb = wh4[2 * cc + 1];
@@ -587,10 +598,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
             const int jj = 8 * cc + 2 * e2;
-            const float x0 = fmaf(dp, wv[2 * e2], fmaf(ds, mv[2 * e2], v[jj]));
-            const float x1 = fmaf(dp, wv[2 * e2 + 1], fmaf(ds, mv[2 * e2 + 1], v[jj + 1]));
-            const float2 f = unpack2<AB16>(dw[e2]);
-            o[e2] = pack2<AB16>(f.x + x0, f.y + x1);
+            o[e2] = pack2<AB16>(fmaf(dp, wv[2 * e2], v[jj]), fmaf(dp, wv[2 * e2 + 1], v[jj + 1]));
           }
           if (valid == B_BT) st_shared_v4(sC + g * 8192 + sw128(t, cc), o[0], o[1], o[2], o[3]);  // staged
           else if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
