@@ -240,6 +240,12 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       for (int i = 0; i < nchunks && ok; ++i) {
         const int s = i & 1;
         const uint32_t st = sbase + s * B_STAGE, sK = st + B_OFF_K;
+        if (i >= 1) {  // carry / dW of the previous chunk first: its R columns are rewritten by E1 of this one
+          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2);
+          if (!ok) break;
+          tc_fence_after();
+          cw(i - 1);
+        }
         ok = pipe_wait(&S.kready[s], (i >> 1) & 1, ab, err, 2) &&
              (i == 0 || pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2));
         if (!ok) break;
@@ -251,10 +257,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
                sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b1, ks > 0);
         umma_commit(&S.da_full);
         if (i >= 1) {
-          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2);
-          if (!ok) break;
-          tc_fence_after();
-          cw(i - 1);
           ok = pipe_wait(&S.c_read, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
           tc_fence_after();
