@@ -34,6 +34,7 @@ FLOP_PER_TH = 339968
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
 # kernel at c2; profiles/tc_fwd_kernel_c2.md and profiles/tc_bwd_kernel_c2.md give the command.
 NCU_TRAFFIC_C2 = {'fwd': 269.0e6 + 110.8e6, 'bwd': 415.5e6 + 231.6e6}
+NCU_TRAFFIC_C4 = 272.7e6 + 214.1e6  # decode_kernel, profiles/decode_kernel_c4.md
 DECODE_BYTES_PER_TH = 2 * 128 * 128 * 4 + 2 * 128 * 4 + 4 * 128 * 2 + 2 * 2
 
 
@@ -380,7 +381,8 @@ def run_decode(args, rank, world, device, hbm_peak, peak_kind):
             'ms_per_step': per * 1e3, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'bf16', 'data': 'synthetic', 'config': {'workload': 'c4: decode batch 256, H=16, d_k=128'},
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s',
-                         'frac': achieved / hbm_peak, 'traffic': None, 'peak_kind': peak_kind},
+                         'frac': achieved / hbm_peak, 'traffic': NCU_TRAFFIC_C4,
+                         'traffic_unit': 'bytes per launch (ncu)', 'peak_kind': peak_kind},
             'clocks': clocks.summary(), 'gpu_launches': n_launch}), flush=True)
 
 
