@@ -147,6 +147,17 @@ def cpu_port_sample(T=4096, Hs=2, K=128, reps=3, warm=1):
     return T * Hs / 16 / t, t, torch.get_num_threads()
 
 
+C2_METRIC = 'CCQ clean fwd+bwd tokens/s/GPU (bf16, T=4096,H=16,dk=128) and % roofline'
+
+
+def c2_config(world, B=8, T=4096, H=16, K=128):
+    """The c2 workload description shared by both arms of the bench."""
+    return {'workload': 'c2: B=8/GPU,T=4096,H=16,d_k=128 cleaning fwd+bwd, per-head gate fused',
+            'global_batch': B * world, 'seq_len': T, 'heads': H, 'd_k': K,
+            'parallelism': f'dp{world} (batch shards, NCCL all-reduce of dW,db)',
+            'l2': 'inputs larger than L2 (q,k,dq_clean 384 MiB per GPU)'}
+
+
 def run_reference(args, rank, world):
     """CPU restatement timed on the host cores (rank 0 only)."""
     if rank != 0:
@@ -162,11 +173,11 @@ def run_reference(args, rank, world):
     value = statistics.median(tps_list) if tps_list else None
     sample = f'B=1,T={T},H={Hs} of 16 heads per step (fp32 torch restatement, chunk 64, autograd); tokens/s scaled by {Hs}/16'
     line = {
-        'impl': 'reference', 'metric': 'CCQ clean fwd+bwd tokens/s/GPU (bf16, T=4096,H=16,dk=128) and % roofline',
+        'impl': 'reference', 'metric': C2_METRIC,
         'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
         'ms_per_step': 32768 / value * 1e3 if value else None, 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'c2: B=8,T=4096,H=16,d_k=128 cleaning fwd+bwd (sampled on CPU)'},
+        'config': c2_config(world),
         'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': thr, 'kind': 'port', 'sample': sample},
         'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
@@ -317,15 +328,12 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0:
         line = {
-            'metric': 'CCQ clean fwd+bwd tokens/s/GPU (bf16, T=4096,H=16,dk=128) and % roofline',
+            'metric': C2_METRIC,
             'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
             'ms_per_step': ms_per_step, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'bf16', 'data': 'synthetic (seeded; q,k unit-normalised N(0,1), W~N(0,0.02), b~U(-1,1))',
-            'config': {'workload': 'c2: B=8/GPU,T=4096,H=16,d_k=128 cleaning fwd+bwd, per-head gate fused',
-                       'global_batch': B * world, 'seq_len': T, 'heads': H, 'd_k': K,
-                       'parallelism': f'dp{world} (batch shards, NCCL all-reduce of dW,db)',
-                       'l2': 'inputs larger than L2 (q,k,dq_clean 384 MiB per GPU)',
-                       'paths': {'fwd': path_fwd, 'bwd': path_bwd}},
+            'config': c2_config(world, B, T, H, K),
+            'paths': {'fwd': path_fwd, 'bwd': path_bwd},
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s',
                          'frac': achieved / hbm_peak, 'traffic': NCU_TRAFFIC_C2['bwd' if dom_bwd else 'fwd'],
                          'traffic_unit': 'bytes per launch (ncu)',
