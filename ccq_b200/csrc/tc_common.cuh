@@ -106,6 +106,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
       ::"r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// tiled prefetch global -> L2 (no shared-memory destination, no barrier): warms a tile that a later
+// load into a still-busy stage will read
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];"
+               ::"l"(tmap), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 // tiled bulk store shared -> global (no multicast); completion tracked per thread by bulk groups
 __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
   asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"

@@ -14,7 +14,10 @@
 // kernel at :86-174).  TMEM holds C (128 columns), two 144-column regions and P' (72 columns of
 // packed 16-bit values, the A operand of F2b); chunk i uses region i % 2 first for its scores A_i
 // and then, once they are read, for Z_i, so the scores of chunk i+1 and the output of chunk i are in
-// flight together.  q_clean is staged in shared memory and written by TMA bulk stores.
+// flight together.  q_clean is staged in shared memory and written by TMA bulk stores; the output
+// group reads q for it again (a TMA load that hits L2) into the staging tile, so an input stage is
+// released as soon as the chunk's last MMA has read it, and the TMA thread also prefetches the next
+// chunk of a stage into L2 while the stage is still busy.
 //
 // Warp roles (640 threads):
 //   warp 0      TMA loads of the Q / K tiles (two stages);
@@ -57,7 +60,7 @@ struct FwdSmall {
   float cf[2][128];        // [chunk parity][row]: lambda_t / pos_t
   float msum[4][128];      // aux: per token-quarter partial key sums
   uint64_t full[2], kready[2], empty[2], a_full[2], a_free[2], cf_ready[2], z_full[2], z_free[2];
-  uint64_t c_full, c_read, cprev_free, cconv, pready, mma_done;
+  uint64_t c_full, c_read, cprev_free, cconv, pready, qo_full, mma_done;
   uint32_t tmem_base;
   int abort;
 };
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.kready[i], 1);
-      mbar_init(&S.empty[i], 2 + GROUP_WARPS);
+      mbar_init(&S.empty[i], 2);  // F2b commit, aux
       mbar_init(&S.a_full[i], 1);
       mbar_init(&S.a_free[i], GROUP_WARPS);
       mbar_init(&S.cf_ready[i], GROUP_WARPS / 2);
@@ -159,6 +162,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     mbar_init(&S.cprev_free, 1);
     mbar_init(&S.cconv, GROUP_WARPS);
     mbar_init(&S.pready, GROUP_WARPS);
+    mbar_init(&S.qo_full, 1);
     mbar_init(&S.mma_done, 1);
     S.abort = 0;
     fence_barrier_init();
@@ -189,6 +193,14 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         tma_load_3d(k_dst, &tmk, &S.full[s], 0, h, row);
         tma_load_3d(k_dst + F_KPANEL, &tmk, &S.full[s], 64, h, row);
         ++issued;
+        // the load of chunk c+2 waits for this stage to be released: warm L2 for it now
+        if (c + 2 < nchunks) {
+          const int prow = (int)(sq.bos + (int64_t)(c + 2) * F_BT);
+          tma_prefetch_3d(&tmq, 0, h, prow);
+          tma_prefetch_3d(&tmq, 64, h, prow);
+          tma_prefetch_3d(&tmk, 0, h, prow);
+          tma_prefetch_3d(&tmk, 64, h, prow);
+        }
       }
       // never leave the CTA with bulk copies in flight
       for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c) mbar_wait(&S.full[c & 1], (c >> 1) & 1);
@@ -391,19 +403,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       nbar_sync(3 + qd, 64);
       const float st = sub_mean ? S.xs[pb][0][t] + S.xs[pb][1][t] : 0.f;
       const float sp = st * ipos;
-      if (hp == 0) {
-        float lamv;
-        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
-        else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
-        S.cf[pb][t] = lamv * ipos;
-        if (a.token_aux && t < valid) {
-          float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
-          *aux = make_float2(lamv, st);
-        }
-        warp_arrive(&S.cf_ready[pb]);
-      }
-      // the P' buffer is free once F2b of the previous chunk has completed
-      if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 16);
+      // P' packed now, stored into TMEM once F2b of the previous chunk has read the buffer
       if (!cols_above) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {  // packed in place: v[i] <- (v[2i], v[2i+1])
@@ -411,12 +411,25 @@ __global__ void __launch_bounds__(F_THREADS, 1)
           const float hi = (cols_below || 64 * hp + 2 * i + 1 <= t) ? v[2 * i + 1] - sp : 0.f;
           v[i] = __uint_as_float(pack2<AB16>(lo, hi));
         }
-        tmem_st32(lrow + T_P + 32 * hp, v);
       }
+      if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 16);
+      if (!cols_above) tmem_st32(lrow + T_P + 32 * hp, v);
       if (hp == 0) tmem_st1(lrow + T_P + 64, pack2<AB16>(-sp, -sp));
       tmem_st_wait();
       tc_fence_before();
       warp_arrive(&S.pready);
+      // lambda / pos for the output group and the token_aux side output, while F2b runs
+      if (hp == 0) {
+        float lamv;
+        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
+        else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
+        S.cf[pb][t] = lamv * ipos;
+        warp_arrive(&S.cf_ready[pb]);
+        if (a.token_aux && t < valid) {
+          float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
+          *aux = make_float2(lamv, st);
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------------ output group: C, q_clean
@@ -475,6 +488,15 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       }
       warp_arrive(&S.cconv);
       // ---------------- q_clean of chunk c = q - (lambda / pos) Z
+      // The Q tile of the stage was released after the chunk's last MMA; q is read again (from L2)
+      // into the staging tile, once the previous bulk store has read that tile.
+      if (leader) {
+        bulk_wait_read();
+        const int row = (int)(sq.bos + (int64_t)t0);
+        mbar_arrive_expect_tx(&S.qo_full, F_QTILE);
+        tma_load_3d(sm + F_OFF_O, &tmq, &S.qo_full, 0, h, row);
+        tma_load_3d(sm + F_OFF_O + F_QPANEL, &tmq, &S.qo_full, 64, h, row);
+      }
       pipe_wait(&S.z_full[s], (c >> 1) & 1, ab, err, 128);
       tc_fence_after();
       tmem_ld64(lrow + T_R + T_RSTRIDE * s + 64 * ho, v);
@@ -482,20 +504,17 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       warp_arrive(&S.z_free[s]);
       pipe_wait(&S.cf_ready[s], (c >> 1) & 1, ab, err, 128);
       const float cf = S.cf[s][r];
-      const uint32_t qpan = sbase + F_OFF_Q + s * F_QTILE + (uint32_t)ho * F_QPANEL;
       const uint32_t opan = sbase + F_OFF_O + (uint32_t)ho * F_QPANEL;
-      // the staging tile is free once the previous bulk store has read it
-      if (leader) bulk_wait_read();
-      nbar_sync(7, 32 * GROUP_WARPS);
+      pipe_wait(&S.qo_full, c & 1, ab, err, 128);  // q of this chunk, reloaded into the staging tile
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        const uint4 qv = ld_shared_v4(qpan + sw128(r, cc));
-        st_shared_v4(opan + sw128(r, cc), sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
+        const uint32_t ad = opan + sw128(r, cc);
+        const uint4 qv = ld_shared_v4(ad);
+        st_shared_v4(ad, sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
                      sub2<AB16>(qv.y, pack2<AB16>(cf * v[8 * cc + 2], cf * v[8 * cc + 3])),
                      sub2<AB16>(qv.z, pack2<AB16>(cf * v[8 * cc + 4], cf * v[8 * cc + 5])),
                      sub2<AB16>(qv.w, pack2<AB16>(cf * v[8 * cc + 6], cf * v[8 * cc + 7])));
       }
-      warp_arrive(&S.empty[s]);  // q of this chunk has been read
       if (valid == F_BT) {
         fence_async_smem();
         nbar_sync(7, 32 * GROUP_WARPS);
