@@ -241,13 +241,13 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         const int s = i & 1;
         const uint32_t st = sbase + s * B_STAGE, sK = st + B_OFF_K;
         if (i >= 1) {  // carry / dW of the previous chunk first: its R columns are rewritten by E1 of this one
-          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2);
+          // CW updates the carry that the previous chunk's dk reads: wait until the epilogue has read it
+          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2) && pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
           tc_fence_after();
           cw(i - 1);
         }
-        ok = pipe_wait(&S.kready[s], (i >> 1) & 1, ab, err, 2) &&
-             (i == 0 || pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2));
+        ok = pipe_wait(&S.kready[s], (i >> 1) & 1, ab, err, 2);
         if (!ok) break;
         tc_fence_after();
         // B1: [D ; A] = [dQc ; Q] K^T
