@@ -53,8 +53,7 @@ struct BwdSmall {
   float wpart[2][64], upart[2][64];
   float w[64], ds[64], dpre[64];
   uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
-  uint64_t tinit, da_full, c_full, c_read, cconv, cprev_free, pdone, gconv, g_full, zq_full, zq_free, dk_full,
-      dk_read, dpre_ready, cw_done, mma_done;
+  uint64_t tinit, da_full, c_full, cconv, g_full, zq_full, dk_full, dk_read, cw_done, mma_done;
   float db;
   uint32_t tmem_base;
   int abort;
@@ -150,10 +149,10 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       mbar_init(&S.m_ready[i], 1);
       mbar_init(&S.m_free[i], EPI_WARPS);
     }
-    uint64_t* ones[] = {&S.da_full, &S.c_full, &S.cprev_free, &S.g_full, &S.zq_full, &S.dk_full, &S.cw_done,
+    uint64_t* ones[] = {&S.da_full, &S.c_full, &S.g_full, &S.zq_full, &S.dk_full, &S.cw_done,
                         &S.mma_done};
     for (uint64_t* b : ones) mbar_init(b, 1);
-    uint64_t* epis[] = {&S.tinit, &S.c_read, &S.cconv, &S.pdone, &S.gconv, &S.zq_free, &S.dk_read, &S.dpre_ready};
+    uint64_t* epis[] = {&S.tinit, &S.cconv, &S.dk_read};
     for (uint64_t* b : epis) mbar_init(b, EPI_WARPS);
     S.abort = 0;
     S.db = 0.f;
@@ -240,9 +239,12 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       for (int i = 0; i < nchunks && ok; ++i) {
         const int s = i & 1;
         const uint32_t st = sbase + s * B_STAGE, sK = st + B_OFF_K;
+        // Every epilogue warp arrives on its barriers in program order (G read, E1 operands stored,
+        // C read, C_prev stored = cconv; ZQ read, dpre stored, dk^T and carry read = dk_read), and a
+        // commit covers every earlier MMA of this thread, so one wait stands for all earlier steps.
         if (i >= 1) {  // carry / dW of the previous chunk first: its R columns are rewritten by E1 of this one
-          // CW updates the carry that the previous chunk's dk reads: wait until the epilogue has read it
-          ok = pipe_wait(&S.dpre_ready, (i - 1) & 1, ab, err, 2) && pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2);
+          // dk_read: the previous chunk's dpre is stored and its dk^T and carry (updated by CW) are read
+          ok = pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
           tc_fence_after();
           cw(i - 1);
@@ -256,18 +258,13 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           umma(tbase + T_DA, sdesc(st + (ks >> 2) * B_QDPANEL + (ks & 3) * 32, 16, 1024),
                sdesc(sK + (ks >> 2) * B_KPANEL + (ks & 3) * 32, 16, 1024), id_b1, ks > 0);
         umma_commit(&S.da_full);
-        if (i >= 1) {
-          ok = pipe_wait(&S.c_read, (i - 1) & 1, ab, err, 2);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        // B5: C -= K^T K  (C_prev of this chunk)
+        // B5: C -= K^T K  (C_prev of this chunk; the epilogue read C before the cconv waited on last chunk)
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma(tbase + T_C, sdesc(sK + ks * 2048, B_KPANEL, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b5, 1);
         umma_commit(&S.c_full);
-        ok = pipe_wait(&S.pdone, i & 1, ab, err, 2) && pipe_wait(&S.cconv, i & 1, ab, err, 2) &&
-             pipe_wait(&S.gconv, i & 1, ab, err, 2) && (i == 0 || pipe_wait(&S.zq_free, (i - 1) & 1, ab, err, 2));
+        // cconv: bf16 G, [tril(A) ; P2], P4, dZ and bf16 C_prev are in shared memory, and ZQ and G are read
+        ok = pipe_wait(&S.cconv, i & 1, ab, err, 2);
         if (!ok) break;
         tc_fence_after();
         // B2 / B2b: [z ; dq] = [Q ; dZ] C_prev + [tril(A) ; P2] K
@@ -279,7 +276,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         for (int ks = 0; ks < 4; ++ks)
           umma(tbase + T_ZQ, sdesc(sAP + ks * 32, 16, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b2, 1);
         umma_commit(&S.zq_full);
-        umma_commit(&S.cprev_free);
         // B3: dk^T = Q^T P2 + dQc^T P4 + G K^T + G^T K^T   (columns shared with [D ; A])
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
@@ -305,8 +301,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         umma_commit(&S.g_full);
       }
       if (ok && nchunks > 0) {
-        ok = pipe_wait(&S.dk_read, (nchunks - 1) & 1, ab, err, 2) &&
-             pipe_wait(&S.dpre_ready, (nchunks - 1) & 1, ab, err, 2);
+        ok = pipe_wait(&S.dk_read, (nchunks - 1) & 1, ab, err, 2);
         if (ok) {
           tc_fence_after();
           cw(nchunks - 1);
@@ -423,6 +418,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       // this token's (lambda, s) from the forward, loaded early so its latency hides behind E0G
       float2 ax = make_float2(0.f, 0.f);
       if (tv) ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
+      pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);  // long done; checked while B4 still runs
       // ---------------- G (after this chunk) -> bf16 operand of B3
       if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
       tc_fence_after();
@@ -430,12 +426,9 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       store_panel_row<AB16>(sG + g * 16384, r, v);
       fence_async_smem();
       tc_fence_before();
-      warp_arrive(&S.gconv);
 
       // ---------------- E1: P2, tril(A), P4, dZ, R columns
-      pipe_wait(&S.da_full, i & 1, ab, err, 32);
-      pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);
-      if (i >= 1) pipe_wait(&S.cw_done, (i - 1) & 1, ab, err, 32);
+      pipe_wait(&S.da_full, i & 1, ab, err, 32);  // also covers the previous chunk's carry / dW MMAs
       tc_fence_after();
       const float lamv = ax.x, sv = sub_mean ? ax.y : 0.f;
       const float ipos = 1.f / position_of(t0 + t, a.position_offset);
@@ -521,15 +514,13 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         if (g == 0) st_shared_u16(sR + 2048 + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
       }
       fence_async_smem();
-      warp_arrive(&S.pdone);
 
       // ---------------- C_prev -> bf16 operand of B2
       pipe_wait(&S.c_full, i & 1, ab, err, 64);
       tc_fence_after();
       tmem_ld64(lrow + T_C + 64 * g, v);
       tc_fence_before();
-      warp_arrive(&S.c_read);
-      if (i >= 1) pipe_wait(&S.cprev_free, (i - 1) & 1, ab, err, 64);
+      // B2 of the previous chunk has read sC: its zq_full was waited on
       if (et == 0) bulk_wait_read();  // the previous chunk's dq bulk store has read sC
       nbar_sync(1, 256);
       store_panel_row<AB16>(sC + g * 16384, r, v);
@@ -541,7 +532,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tc_fence_after();
       tmem_ld64(lrow + T_ZQ + 64 * g, v);
       tc_fence_before();
-      warp_arrive(&S.zq_free);
       if (dside) {
         float uq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -616,7 +606,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           bulk_commit();
         }
       }
-      warp_arrive(&S.dpre_ready);
       warp_arrive(&S.m_free[s]);
 
       // ---------------- E3: dk = dk^T + carry, staged through the K tile

@@ -77,9 +77,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 
 
 // Pipeline wait that never strands a named barrier: once any wait of the CTA has timed out
-// (*abort set), every later wait returns false at once, so all warps still run through the same
-// sequence of named barriers and reach the end of the kernel; a timeout sets *abort and err.
+// (*abort set), every later wait on a phase that has not completed returns false at once, so all
+// warps still run through the same sequence of named barriers and reach the end of the kernel; a
+// timeout sets *abort and err.  A completed phase is seen by a non-blocking probe first (a blocking
+// probe of a completed phase costs ~170 cycles on B200).
 __device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;  // already completed: no blocking probe
   if (*abort) return false;
   if (mbar_wait(bar, parity)) return true;
   *abort = 1;
