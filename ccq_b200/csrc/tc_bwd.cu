@@ -11,16 +11,19 @@
 //   B2b [z ; dq] += [tril(A) ; P2] K                        P2 = (ds_t - alpha_t D)[j <= t]
 //   B3  dk^T     = Q^T P2 + dQc^T P4 + G K^T + G^T K^T      P4 = (beta_t - alpha_t A)[j <= t]
 //   B4  G       += Q^T dZ
-//   CW  [carry | dW] += Q^T [ds | dpre] + dQc^T [beta | 0]   (persistent 16-column accumulator)
+//   CW  X += Q^T R,  Y += dQc^T R,  R = [ds | dpre | beta | 0]  (persistent 2 x 16 columns: carry =
+//       X[0] + Y[2], dW = X[1]; R is double-buffered by chunk parity so CW of a chunk runs after B1 of
+//       the next one)
 // with ds_t = lambda w_t / pos^2, beta_t = lambda s_t / pos^2, w_t = m_t . dqc_t, and
 //   dq_t = dqc_t + ds_t m_prev + [dq]_t (+ dpre_t W_h),  dlambda_t = -dqc_t . z_t / pos + s w / pos^2,
 //   dk_j = [dk^T]_j + carry  (the in-chunk dm suffix is folded into P2 and P4).
 // These are the reference's gradients (ccq/ops/common/fused_read.py:18-25, kernel :177-307,
 // carry :355-376, dC0 / dm0 :420-450).
 //
-// Warp roles (384 threads): warp 0 TMA (it also writes each chunk's dk, staged by the epilogue in
-// the stage's K tile, with a bulk store before reloading the stage), warp 1 TMEM + MMA issue, warps
-// 2-3 aux (partial-chunk key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.
+// Warp roles (384 threads): warp 0 TMA loads, warp 1 TMEM + MMA issue, warps 2-3 aux (partial-chunk
+// key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.  The epilogue writes
+// dq straight from registers (a thread holds a full 128-byte row segment of it) and stages dk in the
+// stage's K tile, which the TMA thread writes out with a bulk store before it reloads the stage.
 #include "args.h"
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -43,7 +46,7 @@ constexpr uint32_t B_OFF_C = 2 * B_STAGE;        // bf16 C_prev, 2 panels of 128
 constexpr uint32_t B_OFF_G = B_OFF_C + 32768;    // bf16 G, 2 panels of 128 rows
 constexpr uint32_t B_OFF_AP = B_OFF_G + 32768;   // [tril(A) ; P2], 128 rows x 64
 constexpr uint32_t B_OFF_P4 = B_OFF_AP + 16384;  // P4, 64 rows x 64
-constexpr uint32_t B_OFF_R = B_OFF_P4 + 8192;    // R1, R2: 16 rows x 64 each (K-major, rows = columns)
+constexpr uint32_t B_OFF_R = B_OFF_P4 + 8192;    // R[2]: 16 rows x 64 each (K-major, rows = columns)
 constexpr uint32_t B_OFF_SMALL = B_OFF_R + 4096; // 225280
 constexpr uint32_t T_C = 0, T_G = 128, T_ZQ = 256, T_DA = 384, T_CW = 448;
 
@@ -96,6 +99,19 @@ __device__ __forceinline__ void tmem_ld2f(uint32_t taddr, float* x) {
   (void)r3;
 }
 
+// the dm carry of this thread's lane: column 0 (Q^T ds) + column 18 (dQc^T beta) of the CW region
+__device__ __forceinline__ float tmem_carry(uint32_t taddr) {
+  uint32_t r0, r1, r2, r3, s0, s1, s2, s3;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%8];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%4, %5, %6, %7}, [%9];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(s0), "=r"(s1), "=r"(s2), "=r"(s3)
+      : "r"(taddr), "r"(taddr + 16));
+  (void)r1; (void)r2; (void)r3; (void)s0; (void)s1; (void)s3;
+  return __uint_as_float(r0) + __uint_as_float(s2);
+}
+
 template <int AB16>
 __device__ __forceinline__ uint32_t to16(float x) {
   if (AB16) return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
@@ -126,8 +142,8 @@ __device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const f
 template <int AB16>
 __global__ void __launch_bounds__(B_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdq,
-                  const __grid_constant__ CUtensorMap tmdk, CleanArgs a, int* err, float* gate_part) {
+                  const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdk, CleanArgs a,
+                  int* err, float* gate_part) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwdSmall& S = *reinterpret_cast<BwdSmall*>(sm + B_OFF_SMALL);
@@ -225,13 +241,13 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
                      sR = sbase + B_OFF_R;
       auto cw = [&](int i) {  // carry / dW accumulation of iteration i
-        const uint32_t st = sbase + (i & 1) * B_STAGE;
+        const uint32_t st = sbase + (i & 1) * B_STAGE, rb = sR + (i & 1) * 2048;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma(tbase + T_CW, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024), sdesc(sR + ks * 32, 16, 1024), id_cw, 1);
+          umma(tbase + T_CW, sdesc(st + 8192 + ks * 2048, B_QDPANEL, 1024), sdesc(rb + ks * 32, 16, 1024), id_cw, 1);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma(tbase + T_CW, sdesc(st + ks * 2048, B_QDPANEL, 1024), sdesc(sR + 2048 + ks * 32, 16, 1024), id_cw, 1);
+          umma(tbase + T_CW + 16, sdesc(st + ks * 2048, B_QDPANEL, 1024), sdesc(rb + ks * 32, 16, 1024), id_cw, 1);
         umma_commit(&S.cw_done);
         umma_commit(&S.empty[i & 1]);
       };
@@ -242,12 +258,11 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         // Every epilogue warp arrives on its barriers in program order (G read, E1 operands stored,
         // C read, C_prev stored = cconv; ZQ read, dpre stored, dk^T and carry read = dk_read), and a
         // commit covers every earlier MMA of this thread, so one wait stands for all earlier steps.
-        if (i >= 1) {  // carry / dW of the previous chunk first: its R columns are rewritten by E1 of this one
-          // dk_read: the previous chunk's dpre is stored and its dk^T and carry (updated by CW) are read
+        if (i >= 1) {
+          // dk_read: the previous chunk's dpre is stored and its dk^T (B1 overwrites those columns)
+          // and carry (CW updates it) are read
           ok = pipe_wait(&S.dk_read, (i - 1) & 1, ab, err, 2);
           if (!ok) break;
-          tc_fence_after();
-          cw(i - 1);
         }
         ok = pipe_wait(&S.kready[s], (i >> 1) & 1, ab, err, 2);
         if (!ok) break;
@@ -263,6 +278,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         for (int ks = 0; ks < 4; ++ks)
           umma(tbase + T_C, sdesc(sK + ks * 2048, B_KPANEL, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b5, 1);
         umma_commit(&S.c_full);
+        if (i >= 1) cw(i - 1);  // carry / dW of the previous chunk (its own R buffer)
         // cconv: bf16 G, [tril(A) ; P2], P4, dZ and bf16 C_prev are in shared memory, and ZQ and G are read
         ok = pipe_wait(&S.cconv, i & 1, ab, err, 2);
         if (!ok) break;
@@ -402,7 +418,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tmem_st32(lrow + T_CW, v);
     }
     if (gate && et < 128) S.wh[et] = a.gate_w[(int64_t)h * 128 + et];
-    st_shared_v4(sR + 16 * et, 0u, 0u, 0u, 0u);  // R1, R2: columns that stay zero
+    st_shared_v4(sR + 16 * et, 0u, 0u, 0u, 0u);  // R[0], R[1]: rows 3-15 stay zero
     fence_async_smem();
     tmem_st_wait();
     tc_fence_before();
@@ -414,6 +430,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const int t0 = c * B_BT;
       const int valid = min(B_BT, sq.len - t0);
       const uint32_t st = sbase + s * B_STAGE;
+      const uint32_t rb = sR + s * 2048;              // this chunk's R buffer
       const bool tv = t < valid;
       // this token's (lambda, s) from the forward, loaded early so its latency hides behind E0G
       float2 ax = make_float2(0.f, 0.f);
@@ -428,7 +445,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tc_fence_before();
 
       // ---------------- E1: P2, tril(A), P4, dZ, R columns
-      pipe_wait(&S.da_full, i & 1, ab, err, 32);  // also covers the previous chunk's carry / dW MMAs
+      pipe_wait(&S.da_full, i & 1, ab, err, 32);
       tc_fence_after();
       const float lamv = ax.x, sv = sub_mean ? ax.y : 0.f;
       const float ipos = 1.f / position_of(t0 + t, a.position_offset);
@@ -486,7 +503,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         if (g == 0) {
           S.w[t] = w;
           S.ds[t] = ds;
-          st_shared_u16(sR + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(ds));
+          st_shared_u16(rb + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(ds));
         }
       } else {
         const float beta = (sub_mean && tv) ? lamv * sv * ipos * ipos : 0.f;
@@ -511,7 +528,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), mul2<AB16>(d.x, na2), mul2<AB16>(d.y, na2),
                        mul2<AB16>(d.z, na2), mul2<AB16>(d.w, na2));
         }
-        if (g == 0) st_shared_u16(sR + 2048 + sw128(0, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
+        if (g == 0) st_shared_u16(rb + sw128(2, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
       }
       fence_async_smem();
 
@@ -521,8 +538,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       tmem_ld64(lrow + T_C + 64 * g, v);
       tc_fence_before();
       // B2 of the previous chunk has read sC: its zq_full was waited on
-      if (et == 0) bulk_wait_read();  // the previous chunk's dq bulk store has read sC
-      nbar_sync(1, 256);
       store_panel_row<AB16>(sC + g * 16384, r, v);
       fence_async_smem();
       warp_arrive(&S.cconv);
@@ -552,7 +567,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           if (gate) dp = tv ? dl * lamv * (1.f - lamv) : 0.f;
           else if (tv && a.dlam) a.dlam[(sq.bos + t0 + t) * H + h] = dl;
           S.dpre[t] = dp;
-          st_shared_u16(sR + sw128(1, t >> 3) + (t & 7) * 2, to16<AB16>(dp));
+          st_shared_u16(rb + sw128(1, t >> 3) + (t & 7) * 2, to16<AB16>(dp));
           db_acc += dp;
         }
       }
@@ -592,35 +607,24 @@ __global__ void __launch_bounds__(B_THREADS, 1)
             const int jj = 8 * cc + 2 * e2;
             o[e2] = pack2<AB16>(fmaf(dp, wv[2 * e2], v[jj]), fmaf(dp, wv[2 * e2 + 1], v[jj + 1]));
           }
-          if (valid == B_BT) st_shared_v4(sC + g * 8192 + sw128(t, cc), o[0], o[1], o[2], o[3]);  // staged
-          else if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+          if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);  // a full 128-byte row segment per thread
         }
       }
-      fence_async_smem();
-      if (valid == B_BT) {  // dq of the chunk is staged in sC (B2 has read C_prev): one bulk store
-        nbar_sync(1, 256);
-        if (et == 0) {
-          const int row = (int)(sq.bos + (int64_t)t0);
-          tma_store_3d(&tmdq, sm + B_OFF_C, 0, h, row);
-          tma_store_3d(&tmdq, sm + B_OFF_C + 8192, 64, h, row);
-          bulk_commit();
-        }
-      }
+      fence_async_smem();  // dpre in R is read by the CW MMAs
       warp_arrive(&S.m_free[s]);
 
       // ---------------- E3: dk = dk^T + carry, staged through the K tile
       pipe_wait(&S.dk_full, i & 1, ab, err, 256);
       tc_fence_after();
       tmem_ld32(lrow + T_DA + 32 * g, v);
-      float cwv[2];
-      tmem_ld2f(lrow + T_CW, cwv);
+      const float carry = tmem_carry(lrow + T_CW);
       tc_fence_before();
       warp_arrive(&S.dk_read);
       {
         const uint32_t kpanel = st + B_OFF_K + (r >> 6) * B_KPANEL + ((r & 7) * 2);
         const uint32_t rc = (r & 63) >> 3;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + cwv[0]));
+        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + carry));
       }
       if (valid < B_BT) {  // a document's last, partial chunk: plain stores of its valid rows
         nbar_sync(1, 256);
@@ -637,7 +641,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       fence_async_smem();  // the staged dk is read by the TMA thread's bulk store
       warp_arrive(&S.empty[s]);
     }
-    if (et == 0) bulk_wait_all();
     // ---------------- per-document outputs
     if (nchunks > 0) {
       pipe_wait(&S.g_full, (nchunks - 1) & 1, ab, err, 512);
@@ -653,7 +656,8 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     {
       float cwv[2];
       tmem_ld2f(lrow + T_CW, cwv);
-      if (g == 0 && a.dinitial_mean) a.dinitial_mean[st_base + r] = cwv[0];
+      const float carry = tmem_carry(lrow + T_CW);
+      if (g == 0 && a.dinitial_mean) a.dinitial_mean[st_base + r] = carry;
       if (g == 0 && gate) gate_part[((int64_t)n * H + h) * 129 + r] = cwv[1];
     }
     if (gate) {
@@ -684,14 +688,12 @@ __global__ void gate_sum_kernel(const float* part, int n_seqs, int H, float* dW,
 
 template <int AB16>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  CUtensorMap tq, tk, tg;
+  CUtensorMap tq, tk, tg, tdk;
   const int64_t rows = (int64_t)a.B * a.T;
   cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, B_BT, AB16 != 0);
   if (e != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tg, a.dq_clean, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
-  CUtensorMap tdq, tdk;
-  if ((e = tc::make_token_map(&tdq, a.dq, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tdk, a.dk, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   int* err = reinterpret_cast<int*>(a.workspace);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
@@ -699,7 +701,7 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
   auto kern = tc_bwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, a, err, part);
+  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdk, a, err, part);
   *launches += 1;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.lambda_mode == LAMBDA_GATE) {
