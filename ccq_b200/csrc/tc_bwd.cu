@@ -142,8 +142,8 @@ __device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const f
 template <int AB16>
 __global__ void __launch_bounds__(B_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdk, CleanArgs a,
-                  int* err, float* gate_part) {
+                  const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdq,
+                  const __grid_constant__ CUtensorMap tmdk, CleanArgs a, int* err, float* gate_part) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwdSmall& S = *reinterpret_cast<BwdSmall*>(sm + B_OFF_SMALL);
@@ -520,7 +520,10 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           st_shared_v4(sAP + sw128(t, 4 * g + q4), am[0], am[1], am[2], am[3]);
           st_shared_v4(sP4 + sw128(t, 4 * g + q4), p4[0], p4[1], p4[2], p4[3]);
         }
-        // dZ = -alpha dqc, packed
+        // dZ = -alpha dqc, packed.  These rows held the previous chunk's dq tile of this warp, staged
+        // for its bulk store: wait until that store has read them.
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
         const uint32_t na2 = pack2<AB16>(na, na);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
@@ -591,6 +594,10 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       if (gate) nbar_sync(tgrp, 128);  // dpre of these tokens is in S.dpre
       if (!dside) {  // + dpre_t W_h, then out
         const float dp = gate ? S.dpre[t] : 0.f;
+        // A full chunk's dq is staged in the other stage's dZ rows (B4 of the previous chunk has read
+        // them; the next chunk's E1, run by this same warp, rewrites them) and each warp writes its
+        // 32 x 64 block with one bulk store.
+        const uint32_t stg = sbase + (s ^ 1) * B_STAGE + g * B_QDPANEL + 16384;
         uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
         const float4* wh4 = reinterpret_cast<const float4*>(S.wh + 64 * g);
 #pragma unroll
@@ -607,7 +614,18 @@ __global__ void __launch_bounds__(B_THREADS, 1)
             const int jj = 8 * cc + 2 * e2;
             o[e2] = pack2<AB16>(fmaf(dp, wv[2 * e2], v[jj]), fmaf(dp, wv[2 * e2 + 1], v[jj + 1]));
           }
-          if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);  // a full 128-byte row segment per thread
+          if (valid == B_BT) st_shared_v4(stg + sw128(t, cc), o[0], o[1], o[2], o[3]);
+          else if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        if (valid == B_BT) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int tw = 32 * (qd - 2);  // this warp's first token of the chunk
+            tma_store_3d(&tmdq, sm + (s ^ 1) * B_STAGE + g * B_QDPANEL + 16384 + tw * 128, 64 * g, h,
+                         (int)(sq.bos + (int64_t)t0 + tw));
+            bulk_commit();
+          }
         }
       }
       fence_async_smem();  // dpre in R is read by the CW MMAs
@@ -641,6 +659,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       fence_async_smem();  // the staged dk is read by the TMA thread's bulk store
       warp_arrive(&S.empty[s]);
     }
+    if (!dside && lane == 0) bulk_wait_all();  // this warp's dq bulk stores
     // ---------------- per-document outputs
     if (nchunks > 0) {
       pipe_wait(&S.g_full, (nchunks - 1) & 1, ab, err, 512);
@@ -688,20 +707,21 @@ __global__ void gate_sum_kernel(const float* part, int n_seqs, int H, float* dW,
 
 template <int AB16>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  CUtensorMap tq, tk, tg, tdk;
+  CUtensorMap tq, tk, tg, tdq, tdk;
   const int64_t rows = (int64_t)a.B * a.T;
   cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, B_BT, AB16 != 0);
   if (e != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tg, a.dq_clean, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tdk, a.dk, rows, a.H, 128, B_BT, AB16 != 0)) != cudaSuccess) return e;
+  if ((e = tc::make_token_map(&tdq, a.dq, rows, a.H, 128, 32, AB16 != 0)) != cudaSuccess) return e;  // per-warp blocks
   int* err = reinterpret_cast<int*>(a.workspace);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
   auto kern = tc_bwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdk, a, err, part);
+  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, a, err, part);
   *launches += 1;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.lambda_mode == LAMBDA_GATE) {
