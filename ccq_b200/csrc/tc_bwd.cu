@@ -65,7 +65,6 @@ constexpr size_t B_SMEM = B_OFF_SMALL + sizeof(BwdSmall) + 1024;
 static_assert(B_SMEM <= 232448, "backward kernel shared memory");
 constexpr int EPI_WARPS = 8;
 
-__device__ __forceinline__ void nbar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -347,7 +346,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         for (int rr = valid; rr < B_BT; ++rr) st_shared_u32(kt + wp * B_KPANEL + sw128(rr, wi >> 2) + (wi & 3) * 4, 0u);
         fence_async_smem();
       }
-      nbar_sync(2, 64);
+      bar_sync<2, 64>();
       if (at == 0) mbar_arrive(&S.kready[s]);
       if (sub_mean) {
         float acc0 = 0.f, acc1 = 0.f;
@@ -364,7 +363,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       if (i >= 2) pipe_wait(&S.m_free[s], ((i - 2) >> 1) & 1, ab, err, 8);
       S.m_buf[s][2 * at] = m0v;
       S.m_buf[s][2 * at + 1] = m1v;
-      nbar_sync(2, 64);
+      bar_sync<2, 64>();
       if (at == 0) {
         mbar_arrive(&S.m_ready[s]);
         mbar_arrive(&S.empty[s]);
@@ -376,8 +375,6 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     const int g = et >> 7;
     const int qd = warp & 3;
     const int r = 32 * qd + lane;
-    const int pair = 3 + qd;                          // warps qd+4 and qd+8 share TMEM lanes
-    const int tgrp = 7 + (qd & 1);                    // z rows t and dq rows t of the same tokens
     const uint32_t lrow = tbase + ((uint32_t)(32 * qd) << 16);
     const uint32_t sC = sbase + B_OFF_C, sG = sbase + B_OFF_G, sAP = sbase + B_OFF_AP, sP4 = sbase + B_OFF_P4,
                    sR = sbase + B_OFF_R;
@@ -484,7 +481,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           wp += (wq[0] + wq[1]) + (wq[2] + wq[3]);
         }
         S.wpart[g][t] = wp;
-        nbar_sync(pair, 64);
+        bar_sync_quad<3, 64>(qd);
         const float w = S.wpart[0][t] + S.wpart[1][t];
         const float ds = (sub_mean && tv) ? lamv * w * ipos * ipos : 0.f;
         const float na = tv ? -alpha : 0.f;
@@ -561,7 +558,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         }
         const float up = (uq[0] + uq[1]) + (uq[2] + uq[3]);
         S.upart[g][t] = up;
-        nbar_sync(pair, 64);
+        bar_sync_quad<3, 64>(qd);
         if (g == 0) {
           const float u = S.upart[0][t] + S.upart[1][t];
           float dl = -u * ipos;
@@ -591,7 +588,10 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           }
         }
       }
-      if (gate) nbar_sync(tgrp, 128);  // dpre of these tokens is in S.dpre
+      if (gate) {  // dpre of these tokens is in S.dpre (z rows t and dq rows t: quadrants qd and qd ^ 2)
+        if (qd & 1) bar_sync<8, 128>();
+        else bar_sync<7, 128>();
+      }
       if (!dside) {  // + dpre_t W_h, then out
         const float dp = gate ? S.dpre[t] : 0.f;
         // A full chunk's dq is staged in the other stage's dZ rows (B4 of the previous chunk has read
@@ -645,7 +645,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + carry));
       }
       if (valid < B_BT) {  // a document's last, partial chunk: plain stores of its valid rows
-        nbar_sync(1, 256);
+        bar_sync<1, 256>();
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
           const int qid = et + 256 * k4;             // 16-byte chunk id: row (64) x panel (2) x chunk (8)
@@ -682,7 +682,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     if (gate) {
       db_acc = warp_sum(db_acc);
       if (lane == 0 && db_acc != 0.f) atomicAdd(&S.db, db_acc);
-      nbar_sync(1, 256);
+      bar_sync<1, 256>();
       if (et == 0) gate_part[((int64_t)n * H + h) * 129 + 128] = S.db;
     }
   }

@@ -286,6 +286,25 @@ __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
   return r;
 }
 
+// Named barriers with the id and thread count as immediates.  A bar.sync whose barrier id came from
+// a register (computed from the warp index) did not keep its id on sm_100a: warps meant for
+// different barriers completed one another's (measured with one CTA, two warps per id, one of them
+// late), so a runtime id goes through a switch of literal ids.
+template <int ID, int N>
+__device__ __forceinline__ void bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(N) : "memory");
+}
+// barrier FIRST + i, i in 0..3 (one per TMEM lane quadrant)
+template <int FIRST, int N>
+__device__ __forceinline__ void bar_sync_quad(int i) {
+  switch (i) {
+    case 0: bar_sync<FIRST, N>(); break;
+    case 1: bar_sync<FIRST + 1, N>(); break;
+    case 2: bar_sync<FIRST + 2, N>(); break;
+    default: bar_sync<FIRST + 3, N>(); break;
+  }
+}
+
 // one arrive per warp on an mbarrier (count = number of arriving warps), after this warp's prior work
 __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
   __syncwarp();

@@ -67,9 +67,6 @@ struct FwdSmall {
 constexpr size_t F_SMEM = F_OFF_SMALL + sizeof(FwdSmall) + 1024;
 static_assert(F_SMEM <= 232448, "forward kernel shared memory");
 
-__device__ __forceinline__ void nbar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -325,7 +322,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         st_shared_u32(kb + sw128(129, ch) + cb, to16<AB16>(r0) | (to16<AB16>(r1) << 16));
       }
       fence_async_smem();
-      nbar_sync(2, 64);
+      bar_sync<2, 64>();
       if (at == 0) mbar_arrive(&S.kready[s]);
       if (sub_mean) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -343,11 +340,11 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) S.msum[tq][8 * cq + i] = acc[i];
-        nbar_sync(2, 64);
+        bar_sync<2, 64>();
         m0v += S.msum[0][2 * at] + S.msum[1][2 * at] + S.msum[2][2 * at] + S.msum[3][2 * at];
         m1v += S.msum[0][2 * at + 1] + S.msum[1][2 * at + 1] + S.msum[2][2 * at + 1] + S.msum[3][2 * at + 1];
       }
-      nbar_sync(2, 64);
+      bar_sync<2, 64>();
       if (at == 0) mbar_arrive(&S.empty[s]);
     }
     if (sub_mean && a.final_mean) {
@@ -399,9 +396,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         for (int i = 0; i < 4; ++i) tr[i] = (tr[i] + tr[i + 4]) + (tr[i + 8] + tr[i + 12]);
         part += (tr[0] + tr[1]) + (tr[2] + tr[3]);
       }
-      S.xs[pb][hp][t] = part;
-      nbar_sync(3 + qd, 64);
-      const float st = sub_mean ? S.xs[pb][0][t] + S.xs[pb][1][t] : 0.f;
+      // s_t = sum of both column halves.  For tokens 0-63 the second half lies above the diagonal and
+      // adds nothing, so quadrants 0-1 need no exchange (and their half-1 warps no s_t at all).
+      float st = 0.f;
+      if (qd >= 2) {
+        S.xs[pb][hp][t] = part;
+        if (qd == 2) bar_sync<5, 64>();
+        else bar_sync<6, 64>();
+        st = S.xs[pb][0][t] + S.xs[pb][1][t];
+      } else {
+        st = part;
+      }
+      if (!sub_mean) st = 0.f;
       const float sp = st * ipos;
       // P' packed now, stored into TMEM once F2b of the previous chunk has read the buffer
       if (!cols_above) {
@@ -517,7 +523,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       }
       if (valid == F_BT) {
         fence_async_smem();
-        nbar_sync(7, 32 * GROUP_WARPS);
+        bar_sync<7, 32 * GROUP_WARPS>();
         if (leader) {
           const int row = (int)(sq.bos + (int64_t)t0);
           tma_store_3d(&tmo, sm + F_OFF_O, 0, h, row);
