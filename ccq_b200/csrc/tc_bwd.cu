@@ -98,6 +98,28 @@ __device__ __forceinline__ void tmem_ld2f(uint32_t taddr, float* x) {
   (void)r3;
 }
 
+// 16 TMEM lanes x 32 columns in the mma-fragment layout (shape 16x256b, 4 repeats): thread t holds
+// lanes t/4 and t/4 + 8 of the 16, columns 8k + 2(t%4) and 8k + 2(t%4) + 1 for k = 0..3, as
+// v[4k], v[4k+1] (lane t/4) and v[4k+2], v[4k+3] (lane t/4 + 8).
+__device__ __forceinline__ void tmem_ld_frag(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// four 8x8 16-bit matrices in the mma-fragment layout stored transposed: thread 8m + i gives the
+// address of stored row i of matrix m, which receives column i of that matrix
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};"
+               ::"r"(addr), "r"(a0), "r"(a1), "r"(a2), "r"(a3) : "memory");
+}
+
 // the dm carry of this thread's lane: column 0 (Q^T ds) + column 18 (dQc^T beta) of the CW region
 __device__ __forceinline__ float tmem_carry(uint32_t taddr) {
   uint32_t r0, r1, r2, r3, s0, s1, s2, s3;
@@ -634,15 +656,29 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       // ---------------- E3: dk = dk^T + carry, staged through the K tile
       pipe_wait(&S.dk_full, i & 1, ab, err, 256);
       tc_fence_after();
-      tmem_ld32(lrow + T_DA + 32 * g, v);
-      const float carry = tmem_carry(lrow + T_CW);
+      tmem_ld_frag(lrow + T_DA + 32 * g, v);                  // dims 32qd + 0..15
+      tmem_ld_frag(lrow + (16u << 16) + T_DA + 32 * g, v + 16);  // dims 32qd + 16..31
+      const float carry = tmem_carry(lrow + T_CW);            // of dim 32qd + lane
       tc_fence_before();
       warp_arrive(&S.dk_read);
-      {
-        const uint32_t kpanel = st + B_OFF_K + (r >> 6) * B_KPANEL + ((r & 7) * 2);
-        const uint32_t rc = (r & 63) >> 3;
+      {  // dk rows (tokens) written as 8 x 8 blocks transposed out of the fragment layout
+        const int mi = lane >> 3, ri = lane & 7;  // this thread addresses row ri of matrix mi
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) st_shared_u16(kpanel + sw128(32 * g + jj, rc), to16<AB16>(v[jj] + carry));
+        for (int b = 0; b < 2; ++b) {
+          const float* f = v + 16 * b;
+          const float cu = __shfl_sync(0xffffffffu, carry, 16 * b + (lane >> 2));
+          const float cl = __shfl_sync(0xffffffffu, carry, 16 * b + 8 + (lane >> 2));
+          const int dd = 32 * qd + 16 * b + 8 * (mi & 1);   // first dim of matrix mi
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int k0 = 2 * h2, kk = k0 + (mi >> 1);      // matrices: (k0, dims +0), (k0, +8), (k0+1, +0), (k0+1, +8)
+            const uint32_t addr = st + B_OFF_K + (dd >> 6) * B_KPANEL + sw128(32 * g + 8 * kk + ri, (dd & 63) >> 3);
+            stmatrix_x4_trans(addr, pack2<AB16>(f[4 * k0] + cu, f[4 * k0 + 1] + cu),
+                              pack2<AB16>(f[4 * k0 + 2] + cl, f[4 * k0 + 3] + cl),
+                              pack2<AB16>(f[4 * k0 + 4] + cu, f[4 * k0 + 5] + cu),
+                              pack2<AB16>(f[4 * k0 + 6] + cl, f[4 * k0 + 7] + cl));
+          }
+        }
       }
       if (valid < B_BT) {  // a document's last, partial chunk: plain stores of its valid rows
         bar_sync<1, 256>();
