@@ -7,7 +7,7 @@
 // ever goes to HBM.  Per chunk, with Q, K, dQc = 64 x 128 tiles, alpha_t = lambda_t / pos_t:
 //   B1  [D ; A]  = [dQc ; Q] K^T                           (M = 128 stacked, N = 64)
 //   B5  C       -= K^T K                                   (-> C_prev)
-//   B2  [z ; dq] = [Q ; dZ] bf16(C_prev)                    dZ = -alpha dQc
+//   B2  [z ; dq] = [0 ; dQc] + [Q ; dZ] bf16(C_prev)        dZ = -alpha dQc (TMEM starts from [0 ; dQc])
 //   B2b [z ; dq] += [tril(A) ; P2] K                        P2 = (ds_t - alpha_t D)[j <= t]
 //   B3  dk^T     = Q^T P2 + dQc^T P4 + G K^T + G^T K^T      P4 = (beta_t - alpha_t A)[j <= t]
 //   B4  G       += Q^T dZ
@@ -15,7 +15,7 @@
 //       X[0] + Y[2], dW = X[1]; R is double-buffered by chunk parity so CW of a chunk runs after B1 of
 //       the next one)
 // with ds_t = lambda w_t / pos^2, beta_t = lambda s_t / pos^2, w_t = m_t . dqc_t, and
-//   dq_t = dqc_t + ds_t m_prev + [dq]_t (+ dpre_t W_h),  dlambda_t = -dqc_t . z_t / pos + s w / pos^2,
+//   dq_t = [dq]_t + ds_t m_prev (+ dpre_t W_h),  dlambda_t = -dqc_t . z_t / pos + s w / pos^2,
 //   dk_j = [dk^T]_j + carry  (the in-chunk dm suffix is folded into P2 and P4).
 // These are the reference's gradients (ccq/ops/common/fused_read.py:18-25, kernel :177-307,
 // carry :355-376, dC0 / dm0 :420-450).
@@ -137,6 +137,18 @@ template <int AB16>
 __device__ __forceinline__ uint32_t to16(float x) {
   if (AB16) return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
   return (uint32_t)__half_as_ushort(__float2half_rn(x));
+}
+
+// 8 packed 16-bit values as fp32
+template <int AB16>
+__device__ __forceinline__ void unpack8(const uint4 v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 p = unpack2<AB16>(w[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
 }
 
 // 8 consecutive 16-bit values of a swizzled panel row, as fp32
@@ -308,7 +320,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           umma(tbase + T_ZQ, sdesc(st + (ks >> 2) * B_QDPANEL + 8192 + (ks & 3) * 32, 16, 1024),
-               sdesc(sC + ks * 2048, 16384, 1024), id_b2, ks > 0);
+               sdesc(sC + ks * 2048, 16384, 1024), id_b2, 1);  // onto the dq_clean / zero start
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma(tbase + T_ZQ, sdesc(sAP + ks * 32, 16, 1024), sdesc(sK + ks * 2048, B_KPANEL, 1024), id_b2, 1);
@@ -549,9 +561,18 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
           st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), mul2<AB16>(d.x, na2), mul2<AB16>(d.y, na2),
                        mul2<AB16>(d.z, na2), mul2<AB16>(d.w, na2));
+          unpack8<AB16>(d, v + 8 * cc);
         }
         if (g == 0) st_shared_u16(rb + sw128(2, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
       }
+      if (dside) {
+#pragma unroll
+        for (int cc = 0; cc < 64; ++cc) v[cc] = 0.f;
+      }
+      // B2 accumulates onto ZQ: its dq rows start from dq_clean (fp32), its z rows from zero
+      tmem_st32(lrow + T_ZQ + 64 * g, v);
+      tmem_st32(lrow + T_ZQ + 64 * g + 32, v + 32);
+      tmem_st_wait();
       fence_async_smem();
 
       // ---------------- C_prev -> bf16 operand of B2
@@ -593,21 +614,15 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           db_acc += dp;
         }
       }
-      if (!dside) {  // dq_t = dqc_t + ds_t m_prev + [dq]_t, before dpre is known
+      if (!dside) {  // dq_t = [dqc_t + dq inter]_t (from ZQ) + ds_t m_prev, before dpre is known
         const float ds = S.ds[t];
         const float4* mp4 = reinterpret_cast<const float4*>(mp + 64 * g);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-          const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
-          const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
           const float4 ma = mp4[2 * cc], mb = mp4[2 * cc + 1];
           const float mv[8] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
 #pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const float2 f = unpack2<AB16>(dw[e2]);
-            v[8 * cc + 2 * e2] = f.x + fmaf(ds, mv[2 * e2], v[8 * cc + 2 * e2]);
-            v[8 * cc + 2 * e2 + 1] = f.y + fmaf(ds, mv[2 * e2 + 1], v[8 * cc + 2 * e2 + 1]);
-          }
+          for (int e = 0; e < 8; ++e) v[8 * cc + e] = fmaf(ds, mv[e], v[8 * cc + e]);
         }
       }
       if (gate) {  // dpre of these tokens is in S.dpre (z rows t and dq rows t: quadrants qd and qd ^ 2)
