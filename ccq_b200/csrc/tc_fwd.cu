@@ -395,6 +395,8 @@ __global__ void __launch_bounds__(F_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) tr[i] = (tr[i] + tr[i + 4]) + (tr[i + 8] + tr[i + 12]);
         part += (tr[0] + tr[1]) + (tr[2] + tr[3]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(pack2<AB16>(v[2 * i], v[2 * i + 1]));
       }
       // s_t = sum of both column halves.  For tokens 0-63 the second half lies above the diagonal and
       // adds nothing, so quadrants 0-1 need no exchange (and their half-1 warps no s_t at all).
@@ -412,9 +414,10 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       // P' packed now, stored into TMEM once F2b of the previous chunk has read the buffer
       if (!cols_above) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {  // packed in place: v[i] <- (v[2i], v[2i+1])
-          const float lo = (cols_below || 64 * hp + 2 * i <= t) ? v[2 * i] - sp : 0.f;
-          const float hi = (cols_below || 64 * hp + 2 * i + 1 <= t) ? v[2 * i + 1] - sp : 0.f;
+        for (int i = 0; i < 32; ++i) {  // repacked in place with the mean term
+          const float2 f = unpack2<AB16>(__float_as_uint(v[i]));
+          const float lo = (cols_below || 64 * hp + 2 * i <= t) ? f.x - sp : 0.f;
+          const float hi = (cols_below || 64 * hp + 2 * i + 1 <= t) ? f.y - sp : 0.f;
           v[i] = __uint_as_float(pack2<AB16>(lo, hi));
         }
       }
