@@ -386,8 +386,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       float part = ext[0] + ext[1];
       if (!cols_above) {
         if (!cols_below) {
+          // This warp's 32 tokens t lie in one 32-column half of its 64 columns (tl < 32 for the whole
+          // warp or for none of it): the other half is all kept or all zero, so 32 columns get a mask.
+          const int tl = t - 64 * hp;
+          if (tl < 32) {
 #pragma unroll
-          for (int jj = 0; jj < 64; ++jj) v[jj] = (64 * hp + jj <= t) ? v[jj] : 0.f;
+            for (int jj = 0; jj < 32; ++jj) v[jj] = (jj <= tl) ? v[jj] : 0.f;
+#pragma unroll
+            for (int jj = 32; jj < 64; ++jj) v[jj] = 0.f;
+          } else {
+#pragma unroll
+            for (int jj = 32; jj < 64; ++jj) v[jj] = (jj <= tl) ? v[jj] : 0.f;
+          }
         }
         float tr[16];
 #pragma unroll
@@ -412,13 +422,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       if (!sub_mean) st = 0.f;
       const float sp = st * ipos;
       // P' packed now, stored into TMEM once F2b of the previous chunk has read the buffer
-      if (!cols_above) {
+      if (!cols_above) {  // minus the mean term, in packed 16-bit arithmetic; zero above the diagonal
+        const uint32_t sp2 = pack2<AB16>(sp, sp);
+        if (cols_below) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {  // repacked in place with the mean term
-          const float2 f = unpack2<AB16>(__float_as_uint(v[i]));
-          const float lo = (cols_below || 64 * hp + 2 * i <= t) ? f.x - sp : 0.f;
-          const float hi = (cols_below || 64 * hp + 2 * i + 1 <= t) ? f.y - sp : 0.f;
-          v[i] = __uint_as_float(pack2<AB16>(lo, hi));
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(sub2<AB16>(__float_as_uint(v[i]), sp2));
+        } else {
+          const int tl = t - 64 * hp;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const uint32_t m = (2 * i + 1 <= tl) ? 0xFFFFFFFFu : ((2 * i <= tl) ? 0x0000FFFFu : 0u);
+            v[i] = __uint_as_float(sub2<AB16>(__float_as_uint(v[i]), sp2) & m);
+          }
         }
       }
       if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 16);
