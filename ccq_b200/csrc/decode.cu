@@ -10,6 +10,8 @@
 // the kernel is a streaming pass: one CTA per (column tile, head, document); each thread keeps
 // RPT rows x 4 columns of the state in registers (128-bit loads/stores), accumulates its share of
 // z, and the partial sums meet in shared memory.  T > 1 keeps the state in registers across tokens.
+#include <cooperative_groups.h>
+
 #include "args.h"
 #include "common.cuh"
 
@@ -127,6 +129,9 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
       if (r < K) *reinterpret_cast<float4*>(a.cov_out + (st + r) * K + v) = c[i];
     }
   }
+  // The column tiles of one (document, head) form a thread-block cluster: every tile has read the
+  // mean state before tile 0 writes it, so mean_out may alias mean_in.
+  if (gridDim.x > 1) cooperative_groups::this_cluster().sync();
   if (a.subtract_mean && a.mean_out && vt == 0) {
     __syncthreads();
     for (int i = tid; i < K; i += DT) a.mean_out[st + i] = s_m[i];
@@ -134,16 +139,33 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
   (void)s_red;
 }
 
+// one launch; the column tiles of a (document, head) run as one cluster (gridDim.x CTAs, <= 8)
+template <typename Tin, int VT, int KMAX>
+cudaError_t launch_tiles(const CleanArgs& a) {
+  const unsigned tiles = (unsigned)((a.K + VT - 1) / VT);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, a.H, a.n_seqs);
+  cfg.blockDim = dim3(DT);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = tiles;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = tiles > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, decode_kernel<Tin, VT, KMAX>, a);
+}
+
 template <typename Tin>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  if (a.K <= 64) {
-    decode_kernel<Tin, 64, 64><<<dim3((a.K + 63) / 64, a.H, a.n_seqs), DT, 0, a.stream>>>(a);
-  } else if (a.K <= 128) {
-    decode_kernel<Tin, 128, 128><<<dim3((a.K + 127) / 128, a.H, a.n_seqs), DT, 0, a.stream>>>(a);
-  } else {
-    decode_kernel<Tin, 64, 256><<<dim3((a.K + 63) / 64, a.H, a.n_seqs), DT, 0, a.stream>>>(a);
-  }
+  cudaError_t e;
+  if (a.K <= 64) e = launch_tiles<Tin, 64, 64>(a);
+  else if (a.K <= 128) e = launch_tiles<Tin, 128, 128>(a);
+  else e = launch_tiles<Tin, 64, 256>(a);
   *launches += 1;
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -297,10 +297,11 @@ def test_decode_against_oracle_bf16():
     assert rel_err(np64(m), mn) <= 1e-5
 
 
-def test_decode_inplace_and_gate():
+@pytest.mark.parametrize('N,H,K', [(3, 2, 64), (8, 4, 256)])
+def test_decode_inplace_and_gate(N, H, K):
+    # K = 256 runs as 4 column tiles per (sequence, head) that share the mean state updated in place
     import ccq_b200
     rng = np.random.default_rng(6)
-    N, H, K = 3, 2, 64
     kk = unit(rng, (N, 10, H, K))
     C0 = np.einsum('nthk,nthv->nhkv', kk, kk)
     m0 = kk.sum(1)
