@@ -77,7 +77,9 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
  *   token_aux: optional [B,T,H,2] f32 output, per token and head the lambda used and
  *     s_t = m_t . q_t; the tensor-core backward reads it back instead of recomputing both.
  *   initial_cov / initial_mean: optional; initial_mean is ignored unless subtract_mean.
- *   final_cov / final_mean: optional outputs (the backward's tensor-core path reads them back).
+ *   final_cov / final_mean: optional outputs (the backward's tensor-core path reads them back);
+ *   they must not alias initial_cov / initial_mean (column tiles of one head read the initial
+ *   state while another tile writes the final one).
  */
 int ccq_clean_fwd(int dtype, int B, int T, int H, int K,
                   const void* q, const void* k,
