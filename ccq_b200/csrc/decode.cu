@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
   for (int i = 0; i < RPT; ++i) {
     const int r = rg + RG * i;
     c[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (a.cov_in && colok && r < K) c[i] = *reinterpret_cast<const float4*>(a.cov_in + (st + r) * K + v);
+    if (a.cov_in && colok && r < K) c[i] = __ldcs(reinterpret_cast<const float4*>(a.cov_in + (st + r) * K + v));
   }
   for (int i = tid; i < K; i += DT) {
     s_m[i] = (a.subtract_mean && a.mean_in) ? a.mean_in[st + i] : 0.f;
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const int r = rg + RG * i;
-      if (r < K) *reinterpret_cast<float4*>(a.cov_out + (st + r) * K + v) = c[i];
+      if (r < K) __stcs(reinterpret_cast<float4*>(a.cov_out + (st + r) * K + v), c[i]);
     }
   }
   // The column tiles of one (document, head) form a thread-block cluster: every tile has read the
