@@ -19,7 +19,9 @@ CCQ_OP_FWD, CCQ_OP_BWD, CCQ_OP_DECODE = 0, 1, 2
 PATHS = {0: 'none', 1: 'simt', 2: 'tcgen05', 3: 'decode'}
 
 EXPORTS = ('ccq_last_error', 'ccq_last_path', 'ccq_version', 'ccq_last_launch_count',
-           'ccq_workspace_size', 'ccq_clean_fwd', 'ccq_clean_bwd', 'ccq_decode_step', 'ccq_clean_bwd_noalloc')
+           'ccq_workspace_size', 'ccq_workspace_size_for', 'ccq_device_status', 'ccq_clean_fwd', 'ccq_clean_bwd',
+           'ccq_decode_step', 'ccq_clean_bwd_noalloc', 'ccq_noalloc_status')
+CCQ_WS_HAVE_FWD_OUTPUTS = 1
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -31,6 +33,9 @@ _SIGS = {
     'ccq_version': (_I, []),
     'ccq_last_launch_count': (_I, []),
     'ccq_workspace_size': (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
+    'ccq_workspace_size_for': (_SZ, [_I, _I, _I, _I, _I, _I, _I, _I]),
+    'ccq_device_status': (_I, [_P, _P, ctypes.POINTER(_I)]),
+    'ccq_noalloc_status': (_I, [_P, ctypes.POINTER(_I)]),
     'ccq_clean_fwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P,
                            _P, _SZ, _P]),
     'ccq_clean_bwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P,

@@ -49,6 +49,9 @@ struct CleanArgs {
   void* workspace;
   size_t workspace_bytes;
   cudaStream_t stream;
+  // tensor-core kernels: varlen launch order (device, [n_seqs]; nullptr = document order), set by
+  // the launchers from the workspace
+  const int* doc_order;
 };
 
 // Workspace carving: every region starts on a 256-byte boundary.
@@ -64,6 +67,10 @@ cudaError_t decode_step(const CleanArgs& a, int* launches);
 
 // tensor-core path (bf16/fp16, K == 128)
 bool tc_supported(const CleanArgs& a, int op);
+// Longest-first launch order of varlen documents: bytes it needs in a workspace (0 when the batch
+// gets no reordering) and the kernel that writes it.
+size_t lpt_order_bytes(int n_seqs, bool varlen);
+cudaError_t lpt_order(const CleanArgs& a, int* order, int* launches);
 size_t tc_fwd_workspace(int B, int T, int H, int K, int n_seqs);
 size_t tc_bwd_workspace(int B, int T, int H, int K, int n_seqs);
 cudaError_t tc_fwd(const CleanArgs& a, int* launches);

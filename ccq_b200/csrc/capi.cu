@@ -1,8 +1,8 @@
 // C ABI of the B200 CCQ cleaning operator: argument validation, dispatch and error reporting.
 // Declarations and contracts: include/ccq_b200.h.
 #include <stdarg.h>
-#include <mutex>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "../../include/ccq_b200.h"
@@ -24,6 +24,35 @@ int fail(int code, const char* fmt, ...) {
 
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(CCQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// The tensor-core kernels' error word (word 0 of the workspace they were given): 0, or the OR of
+// the codes of the pipeline waits that gave up.  Copied to the host after the stream drains.
+int read_device_word(const void* ws, cudaStream_t stream, int* code) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, ws, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  *code = v;
+  return CCQ_OK;
+}
+
+// With CCQ_B200_CHECK=1 in the environment every tensor-core call waits for its kernels and returns
+// CCQ_ERR_CUDA if one of their bounded pipeline waits gave up (or the launch failed asynchronously).
+bool check_mode() {
+  const char* env = getenv("CCQ_B200_CHECK");
+  return env && env[0] == '1';
+}
+
+int checked_finish(const char* what, const void* ws, cudaStream_t stream) {
+  if (!check_mode()) return CCQ_OK;
+  int code = 0;
+  int st = read_device_word(ws, stream, &code);
+  if (st != CCQ_OK) return st;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  if (code != 0) return fail(CCQ_ERR_CUDA, "%s: device pipeline timeout, code %#x", what, code);
+  return CCQ_OK;
 }
 
 int check_common(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
@@ -75,6 +104,15 @@ int ccq_last_launch_count(void) { return g_launches; }
 int ccq_version(void) { return 100; }
 
 size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_seqs) {
+  if (op == CCQ_OP_BWD) {
+    const size_t s = ccq_workspace_size_for(op, dtype, B, T, H, K, n_seqs, 0);
+    const size_t t = ccq_workspace_size_for(op, dtype, B, T, H, K, n_seqs, CCQ_WS_HAVE_FWD_OUTPUTS);
+    return s > t ? s : t;
+  }
+  return ccq_workspace_size_for(op, dtype, B, T, H, K, n_seqs, 0);
+}
+
+size_t ccq_workspace_size_for(int op, int dtype, int B, int T, int H, int K, int n_seqs, int flags) {
   if (B < 1 || T < 0 || H < 1 || K < 1 || K > 256 || n_seqs < 1) return 0;
   ccq::CleanArgs a;
   memset(&a, 0, sizeof(a));
@@ -83,14 +121,17 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
     return ccq::tc_supported(a, CCQ_OP_FWD) ? ccq::tc_fwd_workspace(B, T, H, K, n_seqs) : 0;
   }
   if (op == CCQ_OP_BWD) {
-    size_t s = ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
-    if (ccq::tc_supported(a, CCQ_OP_BWD)) {
-      size_t t = ccq::tc_bwd_workspace(B, T, H, K, n_seqs);
-      if (t > s) s = t;
-    }
-    return s;
+    if ((flags & CCQ_WS_HAVE_FWD_OUTPUTS) && ccq::tc_supported(a, CCQ_OP_BWD))
+      return ccq::tc_bwd_workspace(B, T, H, K, n_seqs);
+    return ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
   }
   return 0;
+}
+
+int ccq_device_status(const void* workspace, void* stream, int* code) {
+  g_err[0] = 0;
+  if (workspace == nullptr || code == nullptr) return fail(CCQ_ERR_INVALID, "workspace and code are required");
+  return read_device_word(workspace, (cudaStream_t)stream, code);
 }
 
 int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
@@ -126,6 +167,7 @@ int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   }
   if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_fwd launch");
   g_launches = launches;
+  if (g_path == CCQ_PATH_TCGEN05 && workspace != nullptr) return checked_finish("ccq_clean_fwd", workspace, a.stream);
   return CCQ_OK;
 }
 
@@ -178,6 +220,7 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   }
   if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd launch");
   g_launches = launches;
+  if (tc && workspace != nullptr) return checked_finish("ccq_clean_bwd", workspace, a.stream);
   return CCQ_OK;
 }
 
@@ -219,29 +262,31 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[CCQ_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kNoallocMaxDevices = 64;
-void* g_noalloc_ptr[kNoallocMaxDevices] = {};
-std::mutex g_noalloc_mu;
-
-int noalloc_scratch(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= kNoallocMaxDevices)
-    return fail(CCQ_ERR_UNSUPPORTED, "ccq_clean_bwd_noalloc: device %d, supported are devices 0..%d", dev,
-                kNoallocMaxDevices - 1);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd_noalloc: cudaGetSymbolAddress of the scratch");
-    g_noalloc_ptr[dev] = p;
+// Device address of the scratch on the current device.  Looked up on every call (a cheap runtime
+// query) rather than cached, so a call made under another context of the device, or after
+// cudaDeviceReset, never uses an address from an earlier context.
+int noalloc_scratch(void** out, const char* who) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) {
+    char what[128];
+    snprintf(what, sizeof(what), "%s: cudaGetSymbolAddress of the scratch", who);
+    return cuda_fail(e, what);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return CCQ_OK;
 }
 
 }  // namespace
+
+extern "C" int ccq_noalloc_status(void* stream, int* code) {
+  g_err[0] = 0;
+  if (code == nullptr) return fail(CCQ_ERR_INVALID, "code is required");
+  void* scratch = nullptr;
+  int st = noalloc_scratch(&scratch, "ccq_noalloc_status");
+  if (st != CCQ_OK) return st;
+  return read_device_word(scratch, (cudaStream_t)stream, code);
+}
 
 extern "C" int ccq_clean_bwd_noalloc(int dtype, int B, int T, int H, int K, const void* q, const void* k,
                                      int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
@@ -253,7 +298,7 @@ extern "C" int ccq_clean_bwd_noalloc(int dtype, int B, int T, int H, int K, cons
                                      float* dinitial_mean, void* stream) {
   g_err[0] = 0;
   void* scratch = nullptr;
-  int st = noalloc_scratch(&scratch);
+  int st = noalloc_scratch(&scratch, "ccq_clean_bwd_noalloc");
   if (st != CCQ_OK) return st;
   st = ccq_clean_bwd(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs, position_offset,
                      subtract_mean, initial_cov, initial_mean, state_cov, state_mean, token_aux, dq_clean, dfinal_cov,

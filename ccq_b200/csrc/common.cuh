@@ -33,6 +33,9 @@ struct Seq {
   int len;       // tokens in the document
 };
 
+// In the varlen form (B == 1, T = total tokens) every offset is clamped into [0, T] and each end to
+// at least its start, so a malformed cu_seqlens (not starting at 0, decreasing, past the end) gives
+// wrong documents but never an index outside the token tensors or the per-chunk workspaces.
 __device__ __forceinline__ Seq seq_of(int n, int T, const int64_t* cu_seqlens) {
   Seq s;
   if (cu_seqlens == nullptr) {
@@ -40,11 +43,18 @@ __device__ __forceinline__ Seq seq_of(int n, int T, const int64_t* cu_seqlens) {
     s.len = T;
   } else {
     int64_t a = cu_seqlens[n], b = cu_seqlens[n + 1];
+    a = a < 0 ? 0 : (a > T ? T : a);
+    b = b < a ? a : (b > T ? T : b);
     s.bos = a;
     s.len = (int)(b - a);
   }
   return s;
 }
+
+// Varlen launch order: document index of launch slot r, longest document first (LPT), so that a
+// long document does not start in a late wave of CTAs and set the kernel's tail.  `order` is
+// written by lpt_order() (tc.cu); nullptr means launch order = document order.
+__device__ __forceinline__ int doc_of_slot(int r, const int* order) { return order ? order[r] : r; }
 
 // Chunk slot of a document's first chunk in per-chunk workspaces: floor(bos / BT) + n.
 // Slots of consecutive documents never overlap (floor(a) + ceil(b) <= floor(a + b) + 1), and

@@ -40,4 +40,42 @@ bool tc_supported(const CleanArgs& a, int op) {
 }
 
 
+namespace {
+constexpr int kLptMaxDocs = 4096;
+constexpr int kLptThreads = 1024;
+
+// order[rank] = document, ranks by decreasing length (ties: lower index first).  One CTA; each
+// thread ranks its documents against all lengths held in shared memory.
+__global__ void __launch_bounds__(kLptThreads) lpt_order_kernel(const int64_t* cu, int n_seqs, int T, int* order) {
+  __shared__ int len[kLptMaxDocs];
+  for (int d = threadIdx.x; d < n_seqs; d += kLptThreads) {
+    int64_t a = cu[d], b = cu[d + 1];
+    a = a < 0 ? 0 : (a > T ? T : a);
+    b = b < a ? a : (b > T ? T : b);
+    len[d] = (int)(b - a);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < n_seqs; d += kLptThreads) {
+    const int ld = len[d];
+    int rank = 0;
+    for (int e = 0; e < n_seqs; ++e) {
+      const int le = len[e];
+      rank += (le > ld) || (le == ld && e < d);
+    }
+    order[rank] = d;
+  }
+}
+}  // namespace
+
+size_t lpt_order_bytes(int n_seqs, bool varlen) {
+  if (!varlen || n_seqs < 2 || n_seqs > kLptMaxDocs) return 0;
+  return ws_align(sizeof(int) * (size_t)n_seqs);
+}
+
+cudaError_t lpt_order(const CleanArgs& a, int* order, int* launches) {
+  lpt_order_kernel<<<1, kLptThreads, 0, a.stream>>>(a.cu_seqlens, a.n_seqs, a.T, order);
+  *launches += 1;
+  return cudaGetLastError();
+}
+
 }  // namespace ccq

@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
   const uint32_t sbase = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.H;
-  const int h = blockIdx.x % H, n = blockIdx.x / H;
+  const int h = blockIdx.x % H, n = doc_of_slot(blockIdx.x / H, a.doc_order);
   const Seq sq = seq_of(n, a.T, a.cu_seqlens);
   const int nchunks = (sq.len + B_BT - 1) / B_BT;
   const int64_t st_base = ((int64_t)n * H + h) * 128;
@@ -745,6 +745,9 @@ __global__ void __launch_bounds__(B_THREADS, 1)
   }
 }
 
+// gate partials: 128 dW entries and db per (document, head)
+size_t part_bytes(int H, int n_seqs) { return ws_align(sizeof(float) * (size_t)n_seqs * H * 129); }
+
 // dW[h] = sum over documents of the per-CTA partials, db[h] likewise
 __global__ void gate_sum_kernel(const float* part, int n_seqs, int H, float* dW, float* db) {
   const int h = blockIdx.x;
@@ -769,10 +772,17 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
   int* err = reinterpret_cast<int*>(a.workspace);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
+  CleanArgs la = a;
+  la.doc_order = nullptr;
+  if (lpt_order_bytes(a.n_seqs, a.cu_seqlens != nullptr) > 0) {
+    int* order = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.workspace) + 256 + part_bytes(a.H, a.n_seqs));
+    if ((e = lpt_order(a, order, launches)) != cudaSuccess) return e;
+    la.doc_order = order;
+  }
   auto kern = tc_bwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, a, err, part);
+  kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, la, err, part);
   *launches += 1;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (a.lambda_mode == LAMBDA_GATE) {
@@ -785,8 +795,9 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
 
 }  // namespace
 
-size_t tc_bwd_workspace(int, int, int H, int, int n_seqs) {
-  return 256 + ws_align(sizeof(float) * (size_t)n_seqs * H * 129);
+// error word (256 bytes), the per-(document, head) gate partials, then the varlen launch order
+size_t tc_bwd_workspace(int B, int, int H, int, int n_seqs) {
+  return 256 + part_bytes(H, n_seqs) + lpt_order_bytes(n_seqs, B == 1 && n_seqs >= 2);
 }
 
 cudaError_t tc_bwd(const CleanArgs& a, int* launches) {

@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
   const uint32_t sbase = smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.H;
-  const int h = blockIdx.x % H, n = blockIdx.x / H;
+  const int h = blockIdx.x % H, n = doc_of_slot(blockIdx.x / H, a.doc_order);
   const Seq sq = seq_of(n, a.T, a.cu_seqlens);
   const int nchunks = (sq.len + F_BT - 1) / F_BT;
   const int64_t st_base = ((int64_t)n * H + h) * 128;
@@ -580,17 +580,27 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
   if ((e = tc::make_token_map(&to, a.q_clean, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
   int* err = reinterpret_cast<int*>(a.workspace);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
+  CleanArgs la = a;
+  la.doc_order = nullptr;
+  if (lpt_order_bytes(a.n_seqs, a.cu_seqlens != nullptr) > 0) {
+    int* order = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.workspace) + 256);
+    if ((e = lpt_order(a, order, launches)) != cudaSuccess) return e;
+    la.doc_order = order;
+  }
   auto kern = tc_fwd_kernel<AB16>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, to, a, err);
+  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, to, la, err);
   *launches += 1;
   return cudaGetLastError();
 }
 
 }  // namespace
 
-size_t tc_fwd_workspace(int, int, int, int, int) { return 256; }
+// error word (256 bytes), then the varlen launch order
+size_t tc_fwd_workspace(int B, int, int, int, int n_seqs) {
+  return 256 + lpt_order_bytes(n_seqs, B == 1 && n_seqs >= 2);
+}
 
 cudaError_t tc_fwd(const CleanArgs& a, int* launches) {
   return a.dtype == DT_BF16 ? launch<1>(a, launches) : launch<0>(a, launches);

@@ -1,6 +1,6 @@
 """Multi-GPU helpers: shard the cleaning operator over ranks and reduce the gate gradients.
 
-The operator has no data-path exchange (SURVEY §8(e)): every (document, head) pair is
+The operator has no data-path exchange: every (document, head) pair is
 independent and the state never crosses a shard.  Ranks take whole batch rows (dense) or whole
 documents (varlen, longest-processing-time-first by length), so each rank holds all heads of its
 tokens and the per-head gate needs no communication.  The only collective is the sum of the
@@ -62,3 +62,59 @@ def allreduce_gate_grads(dW, db, group=None, async_op=False):
         return finish
     finish()
     return None
+
+
+class GateGradReducer:
+    """Per-step sum of the gate gradients over ranks that the next step's kernels never wait for.
+
+    The backward writes dW [H, K] and db [H] straight into one of ``depth`` flat buffers (``out()``
+    gives the views to pass as its outputs); ``submit()`` starts the all-reduce of that buffer on
+    NCCL's stream and returns at once.  A buffer is written again only ``depth`` steps later, after
+    the compute stream has been made to wait for its previous all-reduce (long finished by then),
+    and ``result()`` waits for the latest one where an optimizer would consume it.  With one rank
+    nothing is communicated and ``result()`` returns the local gradients."""
+
+    def __init__(self, H, K, device, group=None, depth=2):
+        self.H, self.K, self.group = H, K, group
+        self.bufs = [torch.empty(H * K + H, device=device, dtype=torch.float32) for _ in range(depth)]
+        self.works = [None] * depth
+        self.i = 0
+        self.last = None
+
+    def _active(self):
+        return dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1
+
+    def out(self):
+        """(dW, db) views of the next free buffer, for the backward to write into."""
+        j = self.i % len(self.bufs)
+        if self.works[j] is not None:
+            self.works[j].wait()
+            self.works[j] = None
+        b = self.bufs[j]
+        return b[:self.H * self.K].view(self.H, self.K), b[self.H * self.K:]
+
+    def submit(self):
+        """Start the sum of the buffer the backward just wrote."""
+        j = self.i % len(self.bufs)
+        if self._active():
+            self.works[j] = dist.all_reduce(self.bufs[j], group=self.group, async_op=True)
+        self.last = j
+        self.i += 1
+
+    def result(self):
+        """(dW, db) summed over ranks for the latest submitted step."""
+        j = self.last
+        if j is None:
+            return None
+        if self.works[j] is not None:
+            self.works[j].wait()
+            self.works[j] = None
+        b = self.bufs[j]
+        return b[:self.H * self.K].view(self.H, self.K), b[self.H * self.K:]
+
+    def drain(self):
+        """Wait for every all-reduce still in flight (before the process group goes away)."""
+        for j, w in enumerate(self.works):
+            if w is not None:
+                w.wait()
+                self.works[j] = None

@@ -58,12 +58,20 @@ def _state(t, shape):
     return t.detach().float().contiguous()
 
 
-def _seqs(B, cu_seqlens):
+def _seqs(B, cu_seqlens, T=None):
+    """(int64 cu_seqlens, number of documents).  With CCQ_B200_CHECK=1 the offsets are also checked
+    (start at 0, never decrease, end at T), which reads them back to the host."""
     if cu_seqlens is None:
         return None, B
     cu = cu_seqlens.to(torch.int64).contiguous()
     if B != 1:
         raise ValueError(f'varlen inputs (cu_seqlens given) must have batch size 1, got {B}')
+    if cu.ndim != 1 or cu.numel() < 2:
+        raise ValueError('cu_seqlens must be a 1-D tensor with at least two offsets')
+    if T is not None and os.environ.get('CCQ_B200_CHECK') == '1':
+        c = cu.cpu()
+        if int(c[0]) != 0 or int(c[-1]) != T or bool((c[1:] < c[:-1]).any()):
+            raise ValueError(f'cu_seqlens must start at 0, never decrease and end at T={T}')
     return cu, cu.numel() - 1
 
 
@@ -94,21 +102,21 @@ def reduce_lambda_grad(dlam3, lam):
     return dl.to(lam.dtype)
 
 
-def _check_device_error(ws, what):
-    """With CCQ_B200_CHECK=1, synchronise and raise if the kernels flagged a bounded-wait timeout.
-
-    The tensor-core kernels write a non-zero word at the start of their workspace when one of
-    their pipeline waits gives up; normal calls leave it zero."""
-    if ws is None or os.environ.get('CCQ_B200_CHECK') != '1':
-        return
-    torch.cuda.synchronize(ws.device)
-    code = int(ws[:4].view(torch.int32).item())
-    if code:
-        raise _lib.CCQError(_lib.CCQ_ERR_CUDA, f'{what}: device pipeline timeout, code {code:#x}')
+def device_status(ws):
+    """Error word of the tensor-core kernels that last used workspace ``ws`` (0 = every bounded
+    pipeline wait completed).  Waits for the current stream.  With CCQ_B200_CHECK=1 the C entry
+    points check it themselves and the operators raise CCQError on a non-zero code."""
+    if ws is None:
+        return 0
+    code = ctypes.c_int(0)
+    _lib.check(_lib.load().ccq_device_status(_p(ws), _stream(ws.device), ctypes.byref(code)))
+    return code.value
 
 
-def _workspace(op, dtype, B, T, H, K, N, device):
-    nbytes = _lib.load().ccq_workspace_size(op, dtype, B, T, H, K, N)
+def _workspace(op, dtype, B, T, H, K, N, device, flags=0):
+    """A workspace sized for the path the call takes (the tensor-core backward needs a few hundred
+    bytes per (document, head); only the exact backward needs per-chunk state checkpoints)."""
+    nbytes = _lib.load().ccq_workspace_size_for(op, dtype, B, T, H, K, N, flags)
     if nbytes == 0:
         return None, 0
     return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
@@ -131,13 +139,15 @@ def clean_fwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_
                                _p(cu), N, int(position_offset), int(bool(subtract_mean)), _p(h0), _p(m0),
                                _p(qc), _p(fcov), _p(fmean), _p(ws), nbytes, _stream(dev))
     _lib.check(st)
-    _check_device_error(ws, 'ccq_clean_fwd')
     return qc, fcov, fmean, aux
 
 
 def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N, fcov, fmean, aux,
-                  dqc, dfinal_cov, dfinal_mean, want_dlam=True):
-    """One ccq_clean_bwd call; returns (dq, dk, dlam3 | (dW, db), dh0, dm0)."""
+                  dqc, dfinal_cov, dfinal_mean, want_dlam=True, gate_out=None):
+    """One ccq_clean_bwd call; returns (dq, dk, dlam3 | (dW, db), dh0, dm0).
+
+    ``gate_out``: optional contiguous fp32 (dW [H, K], db [H]) tensors the gate gradients are
+    written into (for instance views of a buffer that is all-reduced next)."""
     B, T, H, K = q.shape
     dev = q.device
     dt = _dtype_code(q)
@@ -145,12 +155,20 @@ def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_
     dk = torch.empty_like(k)
     gate = gate_w is not None
     dlam = torch.empty(B, T, H, device=dev, dtype=torch.float32) if (want_dlam and not gate) else None
-    dW = torch.empty_like(gate_w) if gate else None
-    db = torch.empty_like(gate_b) if gate else None
+    if gate and gate_out is not None:
+        dW, db = gate_out
+        if not (dW.is_contiguous() and db.is_contiguous() and dW.dtype == torch.float32 and db.dtype == torch.float32
+                and tuple(dW.shape) == (H, K) and tuple(db.shape) == (H,)):
+            raise ValueError('gate_out must be contiguous fp32 tensors of shapes [H, K] and [H]')
+    else:
+        dW = torch.empty_like(gate_w) if gate else None
+        db = torch.empty_like(gate_b) if gate else None
     dh0 = torch.empty(N, H, K, K, device=dev, dtype=torch.float32) if h0 is not None else None
     use_carry = bool(subtract_mean) or dfinal_mean is not None
     dm0 = torch.empty(N, H, K, device=dev, dtype=torch.float32) if (m0 is not None and use_carry) else None
-    ws, nbytes = _workspace(_lib.CCQ_OP_BWD, dt, B, T, H, K, N, dev)
+    have_fwd = fcov is not None and aux is not None and (fmean is not None or not subtract_mean)
+    ws, nbytes = _workspace(_lib.CCQ_OP_BWD, dt, B, T, H, K, N, dev,
+                            _lib.CCQ_WS_HAVE_FWD_OUTPUTS if have_fwd else 0)
     mode = _lib.CCQ_LAMBDA_GATE if gate else _lib.CCQ_LAMBDA_TOKEN
     lib = _lib.load()
     with torch.cuda.device(dev):
@@ -159,8 +177,6 @@ def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_
                                _p(fmean), _p(aux), _p(dqc), _p(dfinal_cov), _p(dfinal_mean), _p(dq), _p(dk), _p(dlam),
                                _p(dW), _p(db), _p(dh0), _p(dm0), _p(ws), nbytes, _stream(dev))
     _lib.check(st)
-    if _lib.last_path() == 'tcgen05':
-        _check_device_error(ws, 'ccq_clean_bwd')
     return dq, dk, ((dW, db) if gate else dlam), dh0, dm0
 
 
@@ -175,7 +191,7 @@ class FusedCCQCleanRead(torch.autograd.Function):
         q = q.contiguous()
         k = k.contiguous() if k.dtype == q.dtype else k.to(q.dtype).contiguous()
         B, T, H, K = q.shape
-        cu, N = _seqs(B, cu_seqlens)
+        cu, N = _seqs(B, cu_seqlens, T)
         h0 = _state(initial_cov_state, (N, H, K, K))
         m0 = _state(initial_mean_state, (N, H, K)) if subtract_mean else None
         lam3 = reshape_lambda_3d(lambda_h, q)
@@ -236,7 +252,7 @@ class FusedCCQCleanGated(torch.autograd.Function):
             raise ValueError(f'gate_w must be [H, K] = [{H}, {K}] and gate_b [H]')
         W = gate_w.detach().float().contiguous()
         bb = gate_b.detach().float().contiguous()
-        cu, N = _seqs(B, cu_seqlens)
+        cu, N = _seqs(B, cu_seqlens, T)
         h0 = _state(initial_cov_state, (N, H, K, K))
         m0 = _state(initial_mean_state, (N, H, K)) if subtract_mean else None
         qc, fcov, fmean, aux = clean_fwd_raw(q, k, None, W, bb, position_offset, h0, m0, subtract_mean, cu, N)
@@ -296,7 +312,7 @@ def decode_step(q, k, lambda_h, cov_state=None, mean_state=None, *, position_off
     q = q.detach().contiguous()
     k = k.detach().to(q.dtype).contiguous()
     B, T, H, K = q.shape
-    cu, N = _seqs(B, cu_seqlens)
+    cu, N = _seqs(B, cu_seqlens, T)
     dev = q.device
     if cov_state is not None and tuple(cov_state.shape) != (N, H, K, K):
         raise ValueError(f'cov_state has shape {tuple(cov_state.shape)}, expected {(N, H, K, K)}')

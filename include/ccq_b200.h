@@ -22,6 +22,16 @@
  *     workspace sized by ccq_workspace_size().
  *   - Every entry point returns a ccq_status; on failure ccq_last_error() returns a message for
  *     the calling thread.  Calls on different streams from different threads are independent.
+ *   - cu_seqlens must start at 0, never decrease and end at T (the reference's convention).  The
+ *     kernels clamp every offset into [0, T], so a malformed array gives wrong documents but no
+ *     access outside the tensors; the Python layer validates it when CCQ_B200_CHECK=1.
+ *   - Device-side failures: every pipeline wait inside the tensor-core kernels is bounded (about a
+ *     second).  A wait that gives up makes the kernel unwind without hanging and OR a non-zero code
+ *     into the first 4 bytes (an int) of the workspace it was given; the launcher zeroes that word
+ *     first.  The entry points return before the kernels run, so they cannot see it; read it with
+ *     ccq_device_status() (ccq_noalloc_status() for ccq_clean_bwd_noalloc), or set the environment
+ *     variable CCQ_B200_CHECK=1, which makes every tensor-core call wait for its kernels and return
+ *     CCQ_ERR_CUDA with the code in its message.
  */
 #ifndef CCQ_B200_H_
 #define CCQ_B200_H_
@@ -63,11 +73,28 @@ int ccq_version(void);
 int ccq_last_launch_count(void);
 
 /*
- * Bytes of workspace `op` needs for these sizes (0 if none).  total_tokens = B*T.
+ * Bytes of workspace `op` needs for these sizes (0 if none), enough for whichever backward path a
+ * call takes (for CCQ_OP_BWD the larger of the two).  total_tokens = B*T.
  * Replaces the temporaries the reference allocates inside _fused_read_fwd/_fused_read_bwd
  * (fused_read.py:385-394, :413-434).
  */
 size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_seqs);
+
+/*
+ * Bytes of workspace for the path a call with these sizes will take.  flags: CCQ_WS_HAVE_FWD_OUTPUTS
+ * when the backward will be given the forward's state_cov / state_mean / token_aux (the tensor-core
+ * backward then runs where supported and needs a few hundred bytes per (document, head); without
+ * them the exact backward checkpoints a K x K state per chunk).  Same role as ccq_workspace_size.
+ */
+#define CCQ_WS_HAVE_FWD_OUTPUTS 1
+size_t ccq_workspace_size_for(int op, int dtype, int B, int T, int H, int K, int n_seqs, int flags);
+
+/*
+ * Error word of the tensor-core kernels that last used `workspace` on `stream`: waits for the
+ * stream, then stores 0 (no wait gave up) or the OR of the codes of the waits that gave up in *code.
+ * No counterpart in the reference (its Triton kernels have no bounded waits).
+ */
+int ccq_device_status(const void* workspace, void* stream, int* code);
 
 /*
  * Forward: q_clean, and optionally the final cov / mean states.
@@ -124,12 +151,15 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K,
  * Same arguments, outputs and errors as ccq_clean_bwd, minus workspace / workspace_bytes: the
  * scratch is a fixed array of CCQ_NOALLOC_SCRATCH_BYTES (1 MiB) in the library's device data.
  *   - A call whose scratch need, on the path it takes, exceeds 1 MiB fails with CCQ_ERR_WORKSPACE
- *     before anything is launched.  The tensor-core backward (bf16 / fp16, K = 128) needs
- *     256 + 516 * n_seqs * H bytes, so it fits up to n_seqs * H = 2031; the exact fp32 backward's
- *     need grows with the sequence length (ccq_workspace_size bounds both paths from above).
- *   - The first call on each device looks the scratch up (cudaGetSymbolAddress, with that device
- *     current) and may load the library's device code; make that first call before any stream
+ *     before anything is launched.  The tensor-core backward (bf16 / fp16, K = 128) needs about
+ *     256 + 516 * n_seqs * H bytes (plus 4 * n_seqs for a varlen batch), so it fits up to
+ *     n_seqs * H = 2031 for a dense batch; the exact fp32 backward's need grows with the sequence
+ *     length (ccq_workspace_size_for gives either path's need).
+ *   - Every call looks the scratch up on the current device (cudaGetSymbolAddress), and the first
+ *     call on a device may load the library's device code; make that first call before any stream
  *     capture begins.
+ *   - A bounded pipeline wait that gives up writes its code into the scratch's error word, which
+ *     ccq_noalloc_status() reads back.
  *   - All calls on one device share the one scratch array: calls that overlap in time (other
  *     streams, other host threads) race and give wrong results.  Calls issued one after the other
  *     on one stream are safe.
@@ -146,6 +176,13 @@ int ccq_clean_bwd_noalloc(int dtype, int B, int T, int H, int K,
                           const void* dq_clean, const float* dfinal_cov, const float* dfinal_mean,
                           void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
                           float* dinitial_cov, float* dinitial_mean, void* stream);
+
+/*
+ * Error word of the last ccq_clean_bwd_noalloc call on the current device (see "Device-side
+ * failures" above): waits for `stream`, then stores 0 or the timeout code in *code.  Allocates
+ * nothing.  No counterpart in the reference.
+ */
+int ccq_noalloc_status(void* stream, int* code);
 
 /*
  * Recurrent (decode / short prefill) cleaning with the generation cache.

@@ -261,7 +261,7 @@ def lambda_headwise_fwd(q, W, bias):
     """Per-head gate lambda[b,t,h] = sigmoid(W[h] . q[b,t,h] + bias[h]).
 
     This is the block-diagonal form of the layer's ``sigmoid(erase_lambda_proj(q))``
-    (ccq/gdn/layer.py:174, :292) that BASELINE's configs name (W_lambda is H x d_k).
+    (ccq/gdn/layer.py:174, :292) that the benchmark configurations use (W_lambda is H x d_k).
     """
     pre = np.einsum('bthk,hk->bth', np.asarray(q, np.float64), np.asarray(W, np.float64)) + np.asarray(bias, np.float64)
     return 1.0 / (1.0 + np.exp(-pre))

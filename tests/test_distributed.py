@@ -95,3 +95,49 @@ def test_gate_grad_allreduce_matches_single_process():
     for r in range(world):
         assert np.allclose(out[r][0], dW, atol=1e-10)
         assert np.allclose(out[r][1], db, atol=1e-10)
+
+
+def _reducer_worker(rank, world, port, out):
+    import torch.distributed as dist
+
+    from ccq_b200.distributed import GateGradReducer
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        H, K = 3, 4
+        red = GateGradReducer(H, K, torch.device('cpu'), depth=2)
+        got = []
+        for step in range(5):
+            dW, db = red.out()  # the backward writes its gate gradients into these views
+            dW.copy_(torch.full((H, K), float(10 * step + rank)))
+            db.copy_(torch.arange(H, dtype=torch.float32) + 100 * step + rank)
+            red.submit()
+            if step % 2 == 1:  # consume every other step, as an optimizer a step late would
+                rW, rb = red.result()
+                got.append((step, rW.clone().numpy(), rb.clone().numpy()))
+        rW, rb = red.result()
+        got.append((4, rW.clone().numpy(), rb.clone().numpy()))
+        red.drain()
+        out[rank] = got
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gate_grad_reducer_double_buffered_sums():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context('spawn')
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    procs = [ctx.Process(target=_reducer_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    H, K = 3, 4
+    for r in range(world):
+        for step, W, b in out[r]:
+            assert np.allclose(W, np.full((H, K), sum(10 * step + q for q in range(world))))
+            assert np.allclose(b, sum(np.arange(H) + 100 * step + q for q in range(world)))

@@ -1,6 +1,6 @@
 """Parity of the CUDA operator (through the C ABI) with the reference's golden vectors and the oracle.
 
-Bars: fp32 within 1e-5 relative error (max |a - b| / max |b|);
+Bars (the operator's stated tolerances): fp32 within 1e-5 relative error (max |a - b| / max |b|);
 bf16 within 2e-2 max-abs error against the float64 oracle evaluated on the bf16-rounded inputs.
 """
 import numpy as np

@@ -1,7 +1,7 @@
 """The attn_mode drop-in rebinds exactly the reference's names for this path (CPU: wiring only).
 
-The reference package is importable only where its checkout exists (this build's container); on a
-host without it the test is skipped.  Nothing here runs a kernel.
+The reference package is found under baseline/_ref (its pip install) or CCQ_REFERENCE_PATH; where
+neither exists the test is skipped.  Nothing here runs a kernel.
 """
 import contextlib
 import os
@@ -9,13 +9,18 @@ import sys
 
 import pytest
 
-REF = os.environ.get('CCQ_REFERENCE_PATH', '/root/reference')
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+from bench import reference_path  # noqa: E402
+
+REF = reference_path()
 
 
 @pytest.fixture
 def ccq_ref():
-    if not os.path.isdir(os.path.join(REF, 'ccq')):
-        pytest.skip('reference checkout not present')
+    if REF is None:
+        pytest.skip('reference package not installed (baseline/_ref or CCQ_REFERENCE_PATH)')
     import torch
     torch.cpu.device = getattr(torch.cpu, 'device', None) or (lambda i=None: contextlib.nullcontext())
     sys.path.insert(0, REF)

@@ -80,8 +80,14 @@ def _rel(a, b):
 def test_noalloc_matches_workspace_entry_point(dtype, gate, shape, tol):
     c = _case(dtype, gate, *shape, seed=7)
     ref = _bwd(c, noalloc=False)
+    from ccq_b200 import _lib
+    lib = _lib.load()
     for _ in range(2):  # two calls in a row reuse the one static scratch
         got = _bwd(c, noalloc=True)
+        # the scratch's error word: every bounded pipeline wait of the call completed
+        code = ctypes.c_int(-1)
+        st = lib.ccq_noalloc_status(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(code))
+        assert st == 0 and code.value == 0, (st, code.value)
         for name in ('dq', 'dk', 'dlam', 'dW', 'db'):
             if ref[name] is None:
                 continue
