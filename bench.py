@@ -527,6 +527,63 @@ def run_c5(args, rank, world, device, hbm_peak, tf_peak, reducer):
             'gpu_launches': launches[0]}
 
 
+def run_c2_l2norm(args, rank, world, device, hbm_peak, tf_peak):
+    """c2 with RAW q and k: the l2norm of both (which the fused_chunk orchestrators apply right before
+    the operator) fused into the kernels, fwd + bwd through the autograd API with the backbone's
+    gradient on the normalised keys; beside it the same step with fla's l2norm as a separate pass
+    (the reference's sequence) in front of this library's operator."""
+    import torch
+
+    import ccq_b200
+    B, T, H, K = 8, 4096, 16, 128
+    gen = torch.Generator(device=device).manual_seed(1500 + rank)
+    q0 = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
+    k0 = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
+    lam0 = torch.rand(B, T, H, generator=gen, device=device).to(torch.bfloat16)
+    dqc = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
+    dkn = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(device)
+
+    def fused():
+        q, k, lam = (t.detach().requires_grad_(True) for t in (q0, k0, lam0))
+        qc, kn, _, _ = ccq_b200.fused_ccq_clean_read_l2norm(q, k, lam)
+        torch.autograd.backward([qc, kn], [dqc, dkn])
+
+    res = {}
+    arms = [('fused', fused)]
+    try:
+        from fla.modules.l2norm import l2norm as fla_l2norm
+
+        def separate():
+            q, k, lam = (t.detach().requires_grad_(True) for t in (q0, k0, lam0))
+            qn, kn = fla_l2norm(q, eps=1e-6), fla_l2norm(k, eps=1e-6)
+            qc, _, _ = ccq_b200.fused_ccq_clean_read(qn, kn, lam)
+            torch.autograd.backward([qc, kn], [dqc, dkn])
+        arms.append(('separate_fla_l2norm', separate))
+    except Exception as exc:
+        res['separate_fla_l2norm'] = {'unavailable': f'{type(exc).__name__}: {exc}'[:200]}
+    for name, fn in arms:
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        el, _ = timed_steps(fn, args.steps, stream)
+        el = max_over_ranks(el, world, device)
+        step_s = el / args.steps
+        res[name] = {'ms_per_step': step_s * 1e3, 'value': B * T * world / step_s, 'unit': 'tokens/s'}
+    # fused path, algorithmic bytes per token-head: fwd reads q, k and writes q_clean, k_norm (+16 B of
+    # per-token side outputs); bwd reads q, k_norm, dq_clean (+16 B), writes dq and dk_norm; the key
+    # gradient then reads dk_norm, the backbone's gradient and k_norm and writes dk
+    th = B * T * H
+    step_bytes = (1040 + 1296 + 1032) * th
+    ach = step_bytes / (res['fused']['ms_per_step'] * 1e-3) / 1e9
+    res['fused']['roofline'] = {'bound': 'hbm', 'achieved': ach, 'peak': hbm_peak, 'unit': 'GB/s',
+                                'frac': ach / hbm_peak, 'bytes_per_token_head': 3368}
+    res['workload'] = ('c2 shapes with raw (un-normalised) bf16 q, k ~ N(0,1), per-token lambda, gradients on '
+                       'q_clean and on the normalised keys; through the autograd API')
+    return res
+
+
 def reference_path():
     """Directory holding the reference package `ccq` (its install under baseline/_ref, or
     CCQ_REFERENCE_PATH), or None."""
@@ -606,6 +663,8 @@ def run_ours(args, rank, world, local_rank):
     try:
         if args.workload in ('all', 'c2'):
             main = run_c2(args, rank, world, device, hbm_peak, tf_peak, peak_kind, reducer)
+        if args.workload in ('all', 'c2'):
+            extra['c2_l2norm'] = run_c2_l2norm(args, rank, world, device, hbm_peak, tf_peak)
         if args.workload in ('all', 'c3'):
             extra['c3'] = run_c3(args, rank, world, device, hbm_peak, tf_peak)
         if args.workload in ('all', 'c4'):

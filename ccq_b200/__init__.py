@@ -2,11 +2,13 @@
 from .ops import (  # noqa: F401
     FusedCCQCleanGated,
     FusedCCQCleanRead,
+    FusedCCQCleanReadL2Norm,
     ccq_gate_lambda,
     decode_step,
     fused_ccq_clean,
     fused_ccq_clean_gated,
     fused_ccq_clean_read,
+    fused_ccq_clean_read_l2norm,
     l2norm,
     reduce_lambda_grad,
     reshape_lambda_3d,

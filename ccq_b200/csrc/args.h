@@ -52,6 +52,18 @@ struct CleanArgs {
   // tensor-core kernels: varlen launch order (device, [n_seqs]; nullptr = document order), set by
   // the launchers from the workspace
   const int* doc_order;
+  // L2 normalisation of q and k inside the operator (the *_l2norm entry points): q and k are the
+  // raw inputs; the forward also writes the normalised keys and the two reciprocal norms per
+  // (token, head); the backward reads the normalised keys as `k`, the saved norms, and the
+  // gradient arriving on the normalised keys from the rest of the model.
+  int qk_norm;
+  void* k_norm;             // fwd output [B,T,H,K]
+  float* norm_aux;          // fwd output [B,T,H,2]: 1/|q|, 1/|k|
+  const float* norm_aux_in; // bwd input, as written by the forward
+  const void* dk_ext;       // bwd input [B,T,H,K] or nullptr
+  // debug only (tensor-core forward): > 0 makes the kernel's first wait give up after that many
+  // cycles, to exercise the bounded-wait error path
+  long long debug_stall_cycles;
 };
 
 // Workspace carving: every region starts on a 256-byte boundary.
@@ -61,6 +73,15 @@ inline size_t ws_align(size_t x) { return (x + 255) & ~size_t(255); }
 size_t simt_bwd_workspace(int B, int T, int H, int K, int n_seqs);
 cudaError_t simt_fwd(const CleanArgs& a, int* launches);
 cudaError_t simt_bwd(const CleanArgs& a, int* launches);
+
+// Row-wise L2 normalisation (l2norm.cu): rows of K elements; r arrays hold two floats per row,
+// `slot` picks which.
+cudaError_t l2norm_rows_fwd(int dtype, const void* x, void* y, float* r_out, int slot, int64_t rows, int K,
+                            cudaStream_t st);
+cudaError_t l2norm_rows_scale(int dtype, const void* x, void* y, const float* r_in, int slot, int64_t rows, int K,
+                              cudaStream_t st);
+cudaError_t l2norm_rows_bwd(int dtype, void* d, const void* d_ext, const void* y, const float* r_in, int slot,
+                            int64_t rows, int K, cudaStream_t st);
 
 // decode step (K % 4 == 0, K <= 256)
 cudaError_t decode_step(const CleanArgs& a, int* launches);

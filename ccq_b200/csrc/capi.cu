@@ -94,6 +94,99 @@ ccq::CleanArgs base_args(int dtype, int B, int T, int H, int K, const void* q, c
   return a;
 }
 
+size_t elem_bytes(int dtype) { return dtype == CCQ_F32 ? 4 : 2; }
+
+// bytes of the normalised-q copy the exact path keeps in the workspace (l2norm entry points only)
+size_t qhat_bytes(const ccq::CleanArgs& a) {
+  return ccq::ws_align((size_t)a.B * a.T * a.H * a.K * elem_bytes(a.dtype));
+}
+
+// Forward dispatch shared by ccq_clean_fwd and ccq_clean_l2norm_fwd.  With qk_norm the tensor-core
+// kernel normalises in its tile loads; the exact path normalises q into the workspace and k into
+// k_norm first, then runs on those.
+int run_fwd(ccq::CleanArgs& a, const char* who) {
+  int launches = 0;
+  cudaError_t e;
+  const bool tc = ccq::tc_supported(a, CCQ_OP_FWD) && (!a.qk_norm || ((uintptr_t)a.k_norm & 15) == 0);
+  if (tc) {
+    size_t need = ccq::tc_fwd_workspace(a.B, a.T, a.H, a.K, a.n_seqs);
+    if (need > 0 && (a.workspace == nullptr || a.workspace_bytes < need))
+      return fail(CCQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, a.workspace_bytes);
+    e = ccq::tc_fwd(a, &launches);
+    g_path = CCQ_PATH_TCGEN05;
+  } else if (a.qk_norm) {
+    const size_t need = qhat_bytes(a);
+    if (a.T > 0 && (a.workspace == nullptr || a.workspace_bytes < need))
+      return fail(CCQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, a.workspace_bytes);
+    const int64_t rows = (int64_t)a.B * a.T * a.H;
+    ccq::CleanArgs b = a;
+    b.q = a.workspace;
+    b.k = a.k_norm;
+    e = ccq::l2norm_rows_fwd(a.dtype, a.q, a.workspace, a.norm_aux, 0, rows, a.K, a.stream);
+    if (e == cudaSuccess) e = ccq::l2norm_rows_fwd(a.dtype, a.k, a.k_norm, a.norm_aux, 1, rows, a.K, a.stream);
+    launches += 2;
+    if (e == cudaSuccess) e = ccq::simt_fwd(b, &launches);
+    g_path = CCQ_PATH_SIMT;
+  } else {
+    e = ccq::simt_fwd(a, &launches);
+    g_path = CCQ_PATH_SIMT;
+  }
+  if (e != cudaSuccess) {
+    char what[96];
+    snprintf(what, sizeof(what), "%s launch", who);
+    return cuda_fail(e, what);
+  }
+  g_launches = launches;
+  if (tc && a.workspace != nullptr) return checked_finish(who, a.workspace, a.stream);
+  return CCQ_OK;
+}
+
+// Backward dispatch shared by ccq_clean_bwd and ccq_clean_l2norm_bwd.
+int run_bwd(ccq::CleanArgs& a, const char* who) {
+  const bool tc = ccq::tc_supported(a, CCQ_OP_BWD) && a.state_cov != nullptr && a.token_aux_in != nullptr &&
+                  (a.state_mean != nullptr || !a.subtract_mean) &&
+                  (!a.qk_norm || (((uintptr_t)a.dk_ext & 15) == 0));
+  const int B = a.B, T = a.T, H = a.H, K = a.K, n = a.n_seqs;
+  size_t need = tc ? ccq::tc_bwd_workspace(B, T, H, K, n) : ccq::simt_bwd_workspace(B, T, H, K, n);
+  const size_t qh = (!tc && a.qk_norm) ? qhat_bytes(a) : 0;
+  need += qh;
+  if (T > 0 && need > 0 && (a.workspace == nullptr || a.workspace_bytes < need))
+    return fail(CCQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", who, need, a.workspace_bytes);
+  int launches = 0;
+  cudaError_t e = cudaSuccess;
+  if (tc) {
+    e = ccq::tc_bwd(a, &launches);
+    g_path = CCQ_PATH_TCGEN05;
+  } else if (a.qk_norm) {
+    // exact path: q_hat recomputed bit for bit from the saved norms, the operator's backward on
+    // (q_hat, k_hat), then both gradients mapped back through the normalisation
+    const int64_t rows = (int64_t)B * T * H;
+    ccq::CleanArgs b = a;
+    b.q = a.workspace;
+    b.workspace = (uint8_t*)a.workspace + qh;
+    b.workspace_bytes = a.workspace_bytes - qh;
+    e = ccq::l2norm_rows_scale(a.dtype, a.q, a.workspace, a.norm_aux_in, 0, rows, K, a.stream);
+    launches += 1;
+    if (e == cudaSuccess) e = ccq::simt_bwd(b, &launches);
+    if (e == cudaSuccess) e = ccq::l2norm_rows_bwd(a.dtype, a.dq, nullptr, a.workspace, a.norm_aux_in, 0, rows, K,
+                                                   a.stream);
+    if (e == cudaSuccess) e = ccq::l2norm_rows_bwd(a.dtype, a.dk, a.dk_ext, a.k, a.norm_aux_in, 1, rows, K, a.stream);
+    launches += 2;
+    g_path = CCQ_PATH_SIMT;
+  } else {
+    e = ccq::simt_bwd(a, &launches);
+    g_path = CCQ_PATH_SIMT;
+  }
+  if (e != cudaSuccess) {
+    char what[96];
+    snprintf(what, sizeof(what), "%s launch", who);
+    return cuda_fail(e, what);
+  }
+  g_launches = launches;
+  if (tc && a.workspace != nullptr) return checked_finish(who, a.workspace, a.stream);
+  return CCQ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -112,18 +205,20 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
   return ccq_workspace_size_for(op, dtype, B, T, H, K, n_seqs, 0);
 }
 
+
 size_t ccq_workspace_size_for(int op, int dtype, int B, int T, int H, int K, int n_seqs, int flags) {
   if (B < 1 || T < 0 || H < 1 || K < 1 || K > 256 || n_seqs < 1) return 0;
   ccq::CleanArgs a;
   memset(&a, 0, sizeof(a));
   a.dtype = dtype; a.B = B; a.T = T; a.H = H; a.K = K; a.n_seqs = n_seqs;
+  const size_t qh = (flags & CCQ_WS_L2NORM) ? qhat_bytes(a) : 0;
   if (op == CCQ_OP_FWD) {
-    return ccq::tc_supported(a, CCQ_OP_FWD) ? ccq::tc_fwd_workspace(B, T, H, K, n_seqs) : 0;
+    return ccq::tc_supported(a, CCQ_OP_FWD) ? ccq::tc_fwd_workspace(B, T, H, K, n_seqs) : qh;
   }
   if (op == CCQ_OP_BWD) {
     if ((flags & CCQ_WS_HAVE_FWD_OUTPUTS) && ccq::tc_supported(a, CCQ_OP_BWD))
       return ccq::tc_bwd_workspace(B, T, H, K, n_seqs);
-    return ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
+    return ccq::simt_bwd_workspace(B, T, H, K, n_seqs) + qh;
   }
   return 0;
 }
@@ -153,22 +248,33 @@ int ccq_clean_fwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   a.final_mean = subtract_mean ? final_mean : nullptr;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
-  int launches = 0;
-  cudaError_t e;
-  if (ccq::tc_supported(a, CCQ_OP_FWD)) {
-    size_t need = ccq::tc_fwd_workspace(B, T, H, K, n_seqs);
-    if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-      return fail(CCQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    e = ccq::tc_fwd(a, &launches);
-    g_path = CCQ_PATH_TCGEN05;
-  } else {
-    e = ccq::simt_fwd(a, &launches);
-    g_path = CCQ_PATH_SIMT;
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_fwd launch");
-  g_launches = launches;
-  if (g_path == CCQ_PATH_TCGEN05 && workspace != nullptr) return checked_finish("ccq_clean_fwd", workspace, a.stream);
-  return CCQ_OK;
+  return run_fwd(a, "ccq_clean_fwd");
+}
+
+int ccq_clean_l2norm_fwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                         const void* lam, const float* gate_w, const float* gate_b, float* token_aux, float* norm_aux,
+                         const int64_t* cu_seqlens, int n_seqs, int position_offset, int subtract_mean,
+                         const float* initial_cov, const float* initial_mean, void* q_clean, void* k_norm,
+                         float* final_cov, float* final_mean, void* workspace, size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  int st = check_common(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
+  if (st != CCQ_OK) return st;
+  if (T > 0 && (q_clean == nullptr || k_norm == nullptr || norm_aux == nullptr))
+    return fail(CCQ_ERR_INVALID, "q_clean, k_norm and norm_aux outputs are required");
+  ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                               position_offset, subtract_mean, stream);
+  a.qk_norm = 1;
+  a.k_norm = k_norm;
+  a.norm_aux = norm_aux;
+  a.token_aux = token_aux;
+  a.initial_cov = initial_cov;
+  a.initial_mean = initial_mean;
+  a.q_clean = q_clean;
+  a.final_cov = final_cov;
+  a.final_mean = subtract_mean ? final_mean : nullptr;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return run_fwd(a, "ccq_clean_l2norm_fwd");
 }
 
 int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
@@ -204,24 +310,47 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K, const void* q, const vo
   a.dinitial_mean = (initial_mean && (subtract_mean || dfinal_mean)) ? dinitial_mean : nullptr;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
-  const bool tc = ccq::tc_supported(a, CCQ_OP_BWD) && state_cov != nullptr && token_aux != nullptr &&
-                  (state_mean != nullptr || !subtract_mean);
-  const size_t need = tc ? ccq::tc_bwd_workspace(B, T, H, K, n_seqs) : ccq::simt_bwd_workspace(B, T, H, K, n_seqs);
-  if (T > 0 && need > 0 && (workspace == nullptr || workspace_bytes < need))
-    return fail(CCQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-  int launches = 0;
-  cudaError_t e;
-  if (tc) {
-    e = ccq::tc_bwd(a, &launches);
-    g_path = CCQ_PATH_TCGEN05;
-  } else {
-    e = ccq::simt_bwd(a, &launches);
-    g_path = CCQ_PATH_SIMT;
-  }
-  if (e != cudaSuccess) return cuda_fail(e, "ccq_clean_bwd launch");
-  g_launches = launches;
-  if (tc && workspace != nullptr) return checked_finish("ccq_clean_bwd", workspace, a.stream);
-  return CCQ_OK;
+  return run_bwd(a, "ccq_clean_bwd");
+}
+
+int ccq_clean_l2norm_bwd(int dtype, int B, int T, int H, int K, const void* q, const void* k_norm, int lambda_mode,
+                         const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens,
+                         int n_seqs, int position_offset, int subtract_mean, const float* initial_cov,
+                         const float* initial_mean, const float* state_cov, const float* state_mean,
+                         const float* token_aux, const float* norm_aux, const void* dq_clean, const void* dk_norm,
+                         const float* dfinal_cov, const float* dfinal_mean, void* dq, void* dk, float* dlam,
+                         float* dgate_w, float* dgate_b, float* dinitial_cov, float* dinitial_mean, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  int st = check_common(dtype, B, T, H, K, q, k_norm, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
+  if (st != CCQ_OK) return st;
+  if (T > 0 && (dq_clean == nullptr || dq == nullptr || dk == nullptr || norm_aux == nullptr))
+    return fail(CCQ_ERR_INVALID, "dq_clean, norm_aux, dq and dk are required");
+  if (lambda_mode == CCQ_LAMBDA_GATE && (dgate_w == nullptr || dgate_b == nullptr))
+    return fail(CCQ_ERR_INVALID, "dgate_w and dgate_b are required in GATE mode");
+  ccq::CleanArgs a = base_args(dtype, B, T, H, K, q, k_norm, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                               position_offset, subtract_mean, stream);
+  a.qk_norm = 1;
+  a.norm_aux_in = norm_aux;
+  a.dk_ext = dk_norm;
+  a.initial_cov = initial_cov;
+  a.initial_mean = initial_mean;
+  a.state_cov = state_cov;
+  a.state_mean = state_mean;
+  a.token_aux_in = token_aux;
+  a.dq_clean = dq_clean;
+  a.dfinal_cov = dfinal_cov;
+  a.dfinal_mean = dfinal_mean;
+  a.dq = dq;
+  a.dk = dk;
+  a.dlam = lambda_mode == CCQ_LAMBDA_TOKEN ? dlam : nullptr;
+  a.dgate_w = dgate_w;
+  a.dgate_b = dgate_b;
+  a.dinitial_cov = initial_cov ? dinitial_cov : nullptr;
+  a.dinitial_mean = (initial_mean && (subtract_mean || dfinal_mean)) ? dinitial_mean : nullptr;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  return run_bwd(a, "ccq_clean_l2norm_bwd");
 }
 
 int ccq_decode_step(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,

@@ -20,6 +20,13 @@
 // These are the reference's gradients (ccq/ops/common/fused_read.py:18-25, kernel :177-307,
 // carry :355-376, dC0 / dm0 :420-450).
 //
+// NORM = 1 (the *_l2norm entry points): q is the raw input and k the forward's normalised keys; the
+// aux warps rescale each chunk's Q rows in shared memory by the forward's 1/|q_t| (the same rounded
+// products the forward formed), and the dq epilogue maps the gradient on the normalised q back
+// through the normalisation, dq = (dq_hat - q_hat (q_hat . dq_hat)) / |q| (fla/modules/l2norm.py:49-72).
+// The gradient on the normalised keys is mapped back by a streaming kernel afterwards (l2norm.cu),
+// once the backbone's share of it has been added.
+//
 // Warp roles (384 threads): warp 0 TMA loads, warp 1 TMEM + MMA issue, warps 2-3 aux (partial-chunk
 // key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.  The epilogue writes
 // dq straight from registers (a thread holds a full 128-byte row segment of it) and stages dk in the
@@ -55,6 +62,7 @@ struct BwdSmall {
   float wh[128];
   float wpart[2][64], upart[2][64];
   float w[64], ds[64], dpre[64];
+  float qdot[2][64];  // NORM: [column half][token] partial q_hat . dq_hat
   uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
   uint64_t tinit, da_full, c_full, cconv, g_full, zq_full, dk_full, dk_read, cw_done, mma_done;
   float db;
@@ -172,7 +180,7 @@ __device__ __forceinline__ void store_panel_row(uint32_t panel, int row, const f
                  pack2<AB16>(v[8 * cc + 4], v[8 * cc + 5]), pack2<AB16>(v[8 * cc + 6], v[8 * cc + 7]));
 }
 
-template <int AB16>
+template <int AB16, int NORM>
 __global__ void __launch_bounds__(B_THREADS, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                   const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmdq,
@@ -372,9 +380,29 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     }
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1, c = nchunks - 1 - i;
+      const int valid = min(B_BT, sq.len - c * B_BT);
+      float rq = 0.f;  // NORM: 1/|q| of token `at` of this chunk, fetched while the loads land
+      if (NORM && at < valid) rq = a.norm_aux_in[((sq.bos + (int64_t)c * B_BT + at) * H + h) * 2];
       pipe_wait(&S.full[s], (i >> 1) & 1, ab, err, 4);
       const uint32_t kt = sbase + s * B_STAGE + B_OFF_K;
-      const int valid = min(B_BT, sq.len - c * B_BT);
+      if (NORM) {  // Q rows (64 + token) of both panels: q_hat = q * (1/|q|), rounded like the forward
+#pragma unroll
+        for (int pn = 0; pn < 2; ++pn) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const uint32_t ad = sbase + s * B_STAGE + pn * B_QDPANEL + sw128(64 + at, cc);
+            const uint4 v4 = ld_shared_v4(ad);
+            uint32_t u[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack2<AB16>(u[j]);
+              u[j] = pack2<AB16>(f.x * rq, f.y * rq);
+            }
+            st_shared_v4(ad, u[0], u[1], u[2], u[3]);
+          }
+        }
+        fence_async_smem();
+      }
       if (valid < B_BT) {
         const uint32_t wp = at >> 5, wi = at & 31;
         for (int rr = valid; rr < B_BT; ++rr) st_shared_u32(kt + wp * B_KPANEL + sw128(rr, wi >> 2) + (wi & 3) * 4, 0u);
@@ -466,6 +494,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       // this token's (lambda, s) from the forward, loaded early so its latency hides behind E0G
       float2 ax = make_float2(0.f, 0.f);
       if (tv) ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
+      const float rqn = (NORM && tv && !dside) ? a.norm_aux_in[((sq.bos + t0 + t) * H + h) * 2] : 0.f;
       pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);  // long done; checked while B4 still runs
       // ---------------- G (after this chunk) -> bf16 operand of B3
       if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
@@ -629,7 +658,60 @@ __global__ void __launch_bounds__(B_THREADS, 1)
         if (qd & 1) bar_sync<8, 128>();
         else bar_sync<7, 128>();
       }
-      if (!dside) {  // + dpre_t W_h, then out
+      if (NORM && !dside) {
+        // dq_hat = v + dpre_t W_h, then dq = (dq_hat - q_hat (q_hat . dq_hat)) / |q|; the dot product
+        // over both column halves meets through shared memory (the two warps of this lane quadrant)
+        const float dp = gate ? S.dpre[t] : 0.f;
+        if (gate) {
+          const float4* wh4 = reinterpret_cast<const float4*>(S.wh + 64 * g);
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const float4 wa = wh4[2 * cc], wb = wh4[2 * cc + 1];
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[8 * cc + e] = fmaf(dp, wv[e], v[8 * cc + e]);
+          }
+        }
+        float qd4[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t qrow = st + g * B_QDPANEL + 8192;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float f[8];
+          ld_row8<AB16>(qrow, t, cc, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qd4[e & 3] = fmaf(f[e], v[8 * cc + e], qd4[e & 3]);
+        }
+        S.qdot[g][t] = (qd4[0] + qd4[1]) + (qd4[2] + qd4[3]);
+        bar_sync_quad<3, 64>(qd);  // ids 5 / 6: the dq-side quadrants 2 and 3
+        const float dot = S.qdot[0][t] + S.qdot[1][t];
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float f[8];
+          ld_row8<AB16>(qrow, t, cc, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[8 * cc + e] = rqn * fmaf(-f[e], dot, v[8 * cc + e]);
+        }
+        const uint32_t stg = sbase + (s ^ 1) * B_STAGE + g * B_QDPANEL + 16384;
+        uint4* orow = reinterpret_cast<uint4*>((uint8_t*)a.dq + (((sq.bos + t0 + t) * H + h) * 128 + 64 * g) * 2);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t o[4];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) o[e2] = pack2<AB16>(v[8 * cc + 2 * e2], v[8 * cc + 2 * e2 + 1]);
+          if (valid == B_BT) st_shared_v4(stg + sw128(t, cc), o[0], o[1], o[2], o[3]);
+          else if (tv) orow[cc] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        if (valid == B_BT) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int tw = 32 * (qd - 2);
+            tma_store_3d(&tmdq, sm + (s ^ 1) * B_STAGE + g * B_QDPANEL + 16384 + tw * 128, 64 * g, h,
+                         (int)(sq.bos + (int64_t)t0 + tw));
+            bulk_commit();
+          }
+        }
+      } else if (!dside) {  // + dpre_t W_h, then out
         const float dp = gate ? S.dpre[t] : 0.f;
         // A full chunk's dq is staged in the other stage's dZ rows (B4 of the previous chunk has read
         // them; the next chunk's E1, run by this same warp, rewrites them) and each warp writes its
@@ -759,7 +841,7 @@ __global__ void gate_sum_kernel(const float* part, int n_seqs, int H, float* dW,
   }
 }
 
-template <int AB16>
+template <int AB16, int NORM>
 cudaError_t launch(const CleanArgs& a, int* launches) {
   CUtensorMap tq, tk, tg, tdq, tdk;
   const int64_t rows = (int64_t)a.B * a.T;
@@ -779,7 +861,7 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
     if ((e = lpt_order(a, order, launches)) != cudaSuccess) return e;
     la.doc_order = order;
   }
-  auto kern = tc_bwd_kernel<AB16>;
+  auto kern = tc_bwd_kernel<AB16, NORM>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM)) != cudaSuccess)
     return e;
   kern<<<a.n_seqs * a.H, B_THREADS, B_SMEM, a.stream>>>(tq, tk, tg, tdq, tdk, la, err, part);
@@ -789,6 +871,11 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
     gate_sum_kernel<<<a.H, 128, 0, a.stream>>>(part, a.n_seqs, a.H, a.dgate_w, a.dgate_b);
     *launches += 1;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (NORM) {  // dk on the normalised keys (+ the backbone's share) -> dk on the raw keys, in place
+    e = l2norm_rows_bwd(a.dtype, a.dk, a.dk_ext, a.k, a.norm_aux_in, 1, rows * a.H, 128, a.stream);
+    *launches += 1;
+    if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -801,7 +888,8 @@ size_t tc_bwd_workspace(int B, int, int H, int, int n_seqs) {
 }
 
 cudaError_t tc_bwd(const CleanArgs& a, int* launches) {
-  return a.dtype == DT_BF16 ? launch<1>(a, launches) : launch<0>(a, launches);
+  if (a.qk_norm) return a.dtype == DT_BF16 ? launch<1, 1>(a, launches) : launch<0, 1>(a, launches);
+  return a.dtype == DT_BF16 ? launch<1, 0>(a, launches) : launch<0, 0>(a, launches);
 }
 
 }  // namespace ccq

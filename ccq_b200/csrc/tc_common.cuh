@@ -90,6 +90,17 @@ __device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// Wait for a copy this CTA issued itself (a TMA load whose bytes always arrive): unlike pipe_wait it
+// keeps waiting after another wait of the CTA gave up, so no copy is ever left in flight into shared
+// memory when the CTA unwinds and exits.  Still bounded (~1 s); a timeout sets *abort and err.
+__device__ __forceinline__ bool own_copy_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  if (mbar_test(bar, parity)) return true;
+  if (mbar_wait(bar, parity)) return true;
+  *abort = 1;
+  atomicOr(err, code);
+  return false;
+}
+
 // ------------------------------------------------------------------------------------------
 // fences
 // ------------------------------------------------------------------------------------------

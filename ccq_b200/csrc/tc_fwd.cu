@@ -29,6 +29,16 @@
 //               the bulk store of each full chunk; a document's last, partial chunk is written with
 //               plain stores so no row of the next document is touched).
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in the workspace and unwinds.
+//
+// NORM = 1 (the *_l2norm entry points) takes raw q and k and applies fla's l2norm (y = x / sqrt(|x|^2
+// + 1e-6), fp32 math, rounded to the activation dtype; fla/modules/l2norm.py:26-46) inside the
+// kernel: the aux warps normalise each chunk's Q and K tiles in place in shared memory before the
+// first MMA reads them, write the normalised keys out (TMA bulk store of the K tile; the backbone
+// reads them next) and the two reciprocal norms per token; the output group renormalises the q it
+// re-reads for q_clean with the same factor, so q_clean = q_hat - (lambda / pos) Z exactly as the
+// reference computes it on l2norm's output.
+#include <stdlib.h>
+
 #include "args.h"
 #include "common.cuh"
 #include "tc_common.cuh"
@@ -59,8 +69,11 @@ struct FwdSmall {
   float xs[2][2][128];     // [chunk parity][column half][row]: partial s_t
   float cf[2][128];        // [chunk parity][row]: lambda_t / pos_t
   float msum[4][128];      // aux: per token-quarter partial key sums
+  float rn[2][2][128];     // NORM: [stage][q | k][row] reciprocal norms of the stage's chunk
+  float rqo[2][128];       // NORM: [chunk parity][row] 1/|q| handed from the score to the output group
   uint64_t full[2], kready[2], empty[2], a_full[2], a_free[2], cf_ready[2], z_full[2], z_free[2];
   uint64_t c_full, c_read, cprev_free, cconv, pready, qo_full, mma_done;
+  uint64_t never;          // debug stall: an mbarrier nothing arrives on
   uint32_t tmem_base;
   int abort;
 };
@@ -126,10 +139,11 @@ __device__ __forceinline__ void store_row64(uint32_t panel, int row, const float
                  pack2<AB16>(x[8 * cc + 4], x[8 * cc + 5]), pack2<AB16>(x[8 * cc + 6], x[8 * cc + 7]));
 }
 
-template <int AB16>
+template <int AB16, int NORM>
 __global__ void __launch_bounds__(F_THREADS, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                  const __grid_constant__ CUtensorMap tmo, CleanArgs a, int* err) {
+                  const __grid_constant__ CUtensorMap tmo, const __grid_constant__ CUtensorMap tmkn, CleanArgs a,
+                  int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   FwdSmall& S = *reinterpret_cast<FwdSmall*>(sm + F_OFF_SMALL);
@@ -160,6 +174,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
     mbar_init(&S.cconv, GROUP_WARPS);
     mbar_init(&S.pready, GROUP_WARPS);
     mbar_init(&S.qo_full, 1);
+    mbar_init(&S.never, 1);
     mbar_init(&S.mma_done, 1);
     S.abort = 0;
     fence_barrier_init();
@@ -170,6 +185,24 @@ __global__ void __launch_bounds__(F_THREADS, 1)
   tc_fence_after();
   const uint32_t tbase = S.tmem_base;
   volatile int* ab = &S.abort;
+
+  if (a.debug_stall_cycles > 0) {
+    // Debug knob (CCQ_B200_DEBUG_STALL_CYCLES): one bounded wait on a barrier nothing arrives on, before
+    // any copy or MMA is issued, so the timeout path (error word, abort flag, every role unwinding
+    // through its named barriers, TMEM freed) runs without a fault or a hang.
+    if (threadIdx.x == 0) {
+      const long long t0 = clock64();
+      while (!mbar_test(&S.never, 0)) {
+        if (clock64() - t0 > a.debug_stall_cycles) {
+          S.abort = 1;
+          atomicOr(err, 0x100);
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    __syncthreads();
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -309,6 +342,67 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       pipe_wait(&S.full[s], (c >> 1) & 1, ab, err, 4);
       const uint32_t kt = sbase + F_OFF_K + s * F_KTILE;
       const int valid = min(F_BT, sq.len - c * F_BT);
+      if (NORM) {
+        // the chunk's 128 q rows, then its 128 k rows, normalised in place: four threads per row
+        // (16-byte chunks 4 sub .. 4 sub + 3 of the row's 16), 16 rows per pass
+        const uint32_t qt = sbase + F_OFF_Q + s * F_QTILE;
+        const int sub = at & 3;
+        const uint32_t pan = sub >> 1, cc0 = (sub & 1) * 4;
+        for (int pass = 0; pass < 16; ++pass) {
+          const int rr = pass * 16 + (at >> 2);
+          const int isk = rr >= 128;
+          const int row = rr & 127;
+          const uint32_t base = isk ? kt + pan * F_KPANEL : qt + pan * F_QPANEL;
+          uint4 w[4];
+          float ss = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            w[i] = ld_shared_v4(base + sw128(row, cc0 + i));
+            const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack2<AB16>(u[j]);
+              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+            }
+          }
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+          const float rinv = 1.0f / sqrtf(ss + 1e-6f);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = unpack2<AB16>(u[j]);
+              o[j] = pack2<AB16>(f.x * rinv, f.y * rinv);
+            }
+            st_shared_v4(base + sw128(row, cc0 + i), o[0], o[1], o[2], o[3]);
+          }
+          if (sub == 0) S.rn[s][isk][row] = rinv;
+        }
+        fence_async_smem();  // normalised tiles -> the MMAs and the bulk store
+        bar_sync<2, 64>();
+        const int t0 = c * F_BT;
+        if (valid == F_BT) {
+          if (at == 0) {
+            const int row0 = (int)(sq.bos + (int64_t)t0);
+            tma_store_3d(&tmkn, sm + F_OFF_K + s * F_KTILE, 0, h, row0);
+            tma_store_3d(&tmkn, sm + F_OFF_K + s * F_KTILE + F_KPANEL, 64, h, row0);
+            bulk_commit();
+          }
+        } else {  // a document's last, partial chunk: plain stores of its valid rows only
+          for (int i = at; i < valid * 16; i += 64) {
+            const int row = i >> 4, pn = (i >> 3) & 1, cc = i & 7;
+            const uint4 val = ld_shared_v4(kt + pn * F_KPANEL + sw128(row, cc));
+            *reinterpret_cast<uint4*>((uint8_t*)a.k_norm + (((sq.bos + t0 + row) * H + h) * 128 + 64 * pn + 8 * cc) * 2) =
+                val;
+          }
+        }
+        for (int t = at; t < valid; t += 64)
+          *reinterpret_cast<float2*>(a.norm_aux + ((sq.bos + t0 + t) * H + h) * 2) =
+              make_float2(S.rn[s][0][t], S.rn[s][1][t]);
+      }
       if (valid < F_BT) {  // keys past the end of the document belong to the next one: zero them
         const uint32_t wp = at >> 5, wi = at & 31;
         for (int rr = valid; rr < F_BT; ++rr) st_shared_u32(kt + wp * F_KPANEL + sw128(rr, wi >> 2) + (wi & 3) * 4, 0u);
@@ -345,8 +439,10 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         m1v += S.msum[0][2 * at + 1] + S.msum[1][2 * at + 1] + S.msum[2][2 * at + 1] + S.msum[3][2 * at + 1];
       }
       bar_sync<2, 64>();
+      if (NORM && at == 0) bulk_wait_read();  // the normalised keys' bulk store has read the stage
       if (at == 0) mbar_arrive(&S.empty[s]);
     }
+    if (NORM && at == 0) bulk_wait_all();
     if (sub_mean && a.final_mean) {
       a.final_mean[st_base + 2 * at] = m0v;
       a.final_mean[st_base + 2 * at + 1] = m1v;
@@ -377,6 +473,8 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       const int valid = min(F_BT, sq.len - t0);
       pipe_wait(&S.a_full[pb], (c >> 1) & 1, ab, err, 16);
       tc_fence_after();
+      // NORM: 1/|q_t| of this chunk, read while the stage still holds it (it is reloaded after F2b)
+      const float rqv = NORM ? S.rn[pb][0][t] : 1.f;
       float ext[4] = {0.f, 0.f, 0.f, 0.f};
       if (!cols_above) tmem_ld64(lrow + T_R + T_RSTRIDE * pb + 64 * hp, v);
       if (hp == 0) tmem_ld4(lrow + T_R + T_RSTRIDE * pb + 128, ext);
@@ -448,6 +546,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
         else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
         S.cf[pb][t] = lamv * ipos;
+        if (NORM) S.rqo[pb][t] = rqv;
         warp_arrive(&S.cf_ready[pb]);
         if (a.token_aux && t < valid) {
           float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
@@ -528,12 +627,22 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       warp_arrive(&S.z_free[s]);
       pipe_wait(&S.cf_ready[s], (c >> 1) & 1, ab, err, 128);
       const float cf = S.cf[s][r];
+      const float rq = NORM ? S.rqo[s][r] : 1.f;
       const uint32_t opan = sbase + F_OFF_O + (uint32_t)ho * F_QPANEL;
-      pipe_wait(&S.qo_full, c & 1, ab, err, 128);  // q of this chunk, reloaded into the staging tile
+      own_copy_wait(&S.qo_full, c & 1, ab, err, 128);  // q of this chunk, reloaded into the staging tile
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         const uint32_t ad = opan + sw128(r, cc);
-        const uint4 qv = ld_shared_v4(ad);
+        uint4 qv = ld_shared_v4(ad);
+        if (NORM) {  // the raw q re-read from memory, normalised exactly as the aux warps did it
+          uint32_t u[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<AB16>(u[j]);
+            u[j] = pack2<AB16>(f.x * rq, f.y * rq);
+          }
+          qv = make_uint4(u[0], u[1], u[2], u[3]);
+        }
         st_shared_v4(ad, sub2<AB16>(qv.x, pack2<AB16>(cf * v[8 * cc], cf * v[8 * cc + 1])),
                      sub2<AB16>(qv.y, pack2<AB16>(cf * v[8 * cc + 2], cf * v[8 * cc + 3])),
                      sub2<AB16>(qv.z, pack2<AB16>(cf * v[8 * cc + 4], cf * v[8 * cc + 5])),
@@ -570,14 +679,30 @@ __global__ void __launch_bounds__(F_THREADS, 1)
   }
 }
 
-template <int AB16>
+// CCQ_B200_DEBUG_STALL_CYCLES=<n> (debug only): the forward kernel's first wait gives up after n
+// clock cycles (at most 2^31), exercising the bounded-wait error path; unset or 0 in normal use.
+long long debug_stall_cycles() {
+  const char* env = getenv("CCQ_B200_DEBUG_STALL_CYCLES");
+  if (env == nullptr) return 0;
+  long long v = atoll(env);
+  if (v < 0) v = 0;
+  if (v > (1ll << 31)) v = 1ll << 31;
+  return v;
+}
+
+template <int AB16, int NORM>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  CUtensorMap tq, tk, to;
+  CUtensorMap tq, tk, to, tkn;
   const int64_t rows = (int64_t)a.B * a.T;
   cudaError_t e = tc::make_token_map(&tq, a.q, rows, a.H, 128, F_BT, AB16 != 0);
   if (e != cudaSuccess) return e;
   if ((e = tc::make_token_map(&tk, a.k, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
   if ((e = tc::make_token_map(&to, a.q_clean, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
+  if (NORM) {
+    if ((e = tc::make_token_map(&tkn, a.k_norm, rows, a.H, 128, F_BT, AB16 != 0)) != cudaSuccess) return e;
+  } else {
+    tkn = tk;  // unused
+  }
   int* err = reinterpret_cast<int*>(a.workspace);
   if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
   CleanArgs la = a;
@@ -587,10 +712,11 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
     if ((e = lpt_order(a, order, launches)) != cudaSuccess) return e;
     la.doc_order = order;
   }
-  auto kern = tc_fwd_kernel<AB16>;
+  la.debug_stall_cycles = debug_stall_cycles();
+  auto kern = tc_fwd_kernel<AB16, NORM>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)F_SMEM)) != cudaSuccess)
     return e;
-  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, to, la, err);
+  kern<<<a.n_seqs * a.H, F_THREADS, F_SMEM, a.stream>>>(tq, tk, to, tkn, la, err);
   *launches += 1;
   return cudaGetLastError();
 }
@@ -603,7 +729,8 @@ size_t tc_fwd_workspace(int B, int, int, int, int n_seqs) {
 }
 
 cudaError_t tc_fwd(const CleanArgs& a, int* launches) {
-  return a.dtype == DT_BF16 ? launch<1>(a, launches) : launch<0>(a, launches);
+  if (a.qk_norm) return a.dtype == DT_BF16 ? launch<1, 1>(a, launches) : launch<0, 1>(a, launches);
+  return a.dtype == DT_BF16 ? launch<1, 0>(a, launches) : launch<0, 0>(a, launches);
 }
 
 }  // namespace ccq

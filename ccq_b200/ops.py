@@ -180,6 +180,59 @@ def clean_bwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_
     return dq, dk, ((dW, db) if gate else dlam), dh0, dm0
 
 
+def clean_l2norm_fwd_raw(q, k, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N):
+    """One ccq_clean_l2norm_fwd call on raw q, k; returns
+    (q_clean, k_norm, final_cov, final_mean, token_aux [B,T,H,2], norm_aux [B,T,H,2])."""
+    B, T, H, K = q.shape
+    dev = q.device
+    dt = _dtype_code(q)
+    qc = torch.empty_like(q)
+    kn = torch.empty_like(k)
+    fcov = torch.empty(N, H, K, K, device=dev, dtype=torch.float32)
+    fmean = torch.empty(N, H, K, device=dev, dtype=torch.float32) if subtract_mean else None
+    aux = torch.empty(B, T, H, 2, device=dev, dtype=torch.float32)
+    naux = torch.empty(B, T, H, 2, device=dev, dtype=torch.float32)
+    ws, nbytes = _workspace(_lib.CCQ_OP_FWD, dt, B, T, H, K, N, dev, _lib.CCQ_WS_L2NORM)
+    mode = _lib.CCQ_LAMBDA_GATE if gate_w is not None else _lib.CCQ_LAMBDA_TOKEN
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.ccq_clean_l2norm_fwd(dt, B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(gate_w), _p(gate_b), _p(aux),
+                                      _p(naux), _p(cu), N, int(position_offset), int(bool(subtract_mean)), _p(h0),
+                                      _p(m0), _p(qc), _p(kn), _p(fcov), _p(fmean), _p(ws), nbytes, _stream(dev))
+    _lib.check(st)
+    return qc, kn, fcov, fmean, aux, naux
+
+
+def clean_l2norm_bwd_raw(q, kn, lam3, gate_w, gate_b, position_offset, h0, m0, subtract_mean, cu, N, fcov, fmean,
+                         aux, naux, dqc, dkn, dfinal_cov, dfinal_mean, want_dlam=True):
+    """One ccq_clean_l2norm_bwd call; returns (dq, dk, dlam3 | (dW, db), dh0, dm0), dq and dk on the raw
+    q and k (``dkn``: gradient arriving on the normalised keys, or None)."""
+    B, T, H, K = q.shape
+    dev = q.device
+    dt = _dtype_code(q)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(kn)
+    gate = gate_w is not None
+    dlam = torch.empty(B, T, H, device=dev, dtype=torch.float32) if (want_dlam and not gate) else None
+    dW = torch.empty_like(gate_w) if gate else None
+    db = torch.empty_like(gate_b) if gate else None
+    dh0 = torch.empty(N, H, K, K, device=dev, dtype=torch.float32) if h0 is not None else None
+    use_carry = bool(subtract_mean) or dfinal_mean is not None
+    dm0 = torch.empty(N, H, K, device=dev, dtype=torch.float32) if (m0 is not None and use_carry) else None
+    ws, nbytes = _workspace(_lib.CCQ_OP_BWD, dt, B, T, H, K, N, dev,
+                            _lib.CCQ_WS_HAVE_FWD_OUTPUTS | _lib.CCQ_WS_L2NORM)
+    mode = _lib.CCQ_LAMBDA_GATE if gate else _lib.CCQ_LAMBDA_TOKEN
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.ccq_clean_l2norm_bwd(dt, B, T, H, K, _p(q), _p(kn), mode, _p(lam3), _p(gate_w), _p(gate_b), _p(cu), N,
+                                      int(position_offset), int(bool(subtract_mean)), _p(h0), _p(m0), _p(fcov),
+                                      _p(fmean), _p(aux), _p(naux), _p(dqc), _p(dkn), _p(dfinal_cov), _p(dfinal_mean),
+                                      _p(dq), _p(dk), _p(dlam), _p(dW), _p(db), _p(dh0), _p(dm0), _p(ws), nbytes,
+                                      _stream(dev))
+    _lib.check(st)
+    return dq, dk, ((dW, db) if gate else dlam), dh0, dm0
+
+
 class FusedCCQCleanRead(torch.autograd.Function):
     """q_clean, final covariance and final key-sum states from (q, k, lambda) (fused_read.py:474-514)."""
 
@@ -236,6 +289,76 @@ def fused_ccq_clean_read(q, k, lambda_h, *, position_offset=0, initial_cov_state
     if not output_final_state:
         final_cov, final_mean = None, None
     return qc, final_cov, final_mean
+
+
+class FusedCCQCleanReadL2Norm(torch.autograd.Function):
+    """l2norm(q), l2norm(k) and the cleaning operator in one: (q_clean, k_norm, final_cov, final_mean)
+    from the raw q and k.  Replaces fla's l2norm of both plus FusedCCQCleanRead as the fused_chunk
+    orchestrators chain them (ccq/ops/ccq_gdn/fused_chunk.py:42-53, ccq/ops/ccq_gla/fused_chunk.py:31-41)."""
+
+    @staticmethod
+    def forward(ctx, q, k, lambda_h, position_offset, initial_cov_state, initial_mean_state,
+                output_final_state, subtract_mean, cu_seqlens):
+        _check_cuda(q, k, lambda_h if isinstance(lambda_h, torch.Tensor) else None,
+                    initial_cov_state, initial_mean_state, cu_seqlens)
+        ctx.set_materialize_grads(False)
+        q = q.contiguous()
+        k = k.contiguous() if k.dtype == q.dtype else k.to(q.dtype).contiguous()
+        B, T, H, K = q.shape
+        cu, N = _seqs(B, cu_seqlens, T)
+        h0 = _state(initial_cov_state, (N, H, K, K))
+        m0 = _state(initial_mean_state, (N, H, K)) if subtract_mean else None
+        lam3 = reshape_lambda_3d(lambda_h, q)
+        qc, kn, fcov, fmean, aux, naux = clean_l2norm_fwd_raw(q, k, lam3, None, None, position_offset, h0, m0,
+                                                              subtract_mean, cu, N)
+        ctx.save_for_backward(q, kn, lam3, h0, m0, cu, fcov, fmean, aux, naux)
+        ctx.lambda_h = lambda_h if isinstance(lambda_h, torch.Tensor) else None
+        ctx.position_offset = int(position_offset)
+        ctx.subtract_mean = bool(subtract_mean)
+        ctx.N = N
+        ctx.has_m0 = initial_mean_state is not None and bool(subtract_mean)
+        if not output_final_state:
+            return qc, kn, None, None
+        return qc, kn, fcov.clone(), (fmean.clone() if fmean is not None else None)
+
+    @staticmethod
+    def backward(ctx, dqc, dkn, dfinal_cov, dfinal_mean):
+        q, kn, lam3, h0, m0, cu, fcov, fmean, aux, naux = ctx.saved_tensors
+        lam_t = ctx.lambda_h
+        need_dl = lam_t is not None and ctx.needs_input_grad[2]
+        if dqc is None:
+            dqc = torch.zeros_like(q)
+        dqc = dqc.contiguous() if dqc.dtype == q.dtype else dqc.to(q.dtype).contiguous()
+        if dkn is not None:
+            dkn = dkn.contiguous() if dkn.dtype == q.dtype else dkn.to(q.dtype).contiguous()
+        dfc = dfinal_cov.float().contiguous() if dfinal_cov is not None else None
+        dfm = dfinal_mean.float().contiguous() if dfinal_mean is not None else None
+        dq, dk, dlam3, dh0, dm0 = clean_l2norm_bwd_raw(q, kn, lam3, None, None, ctx.position_offset, h0, m0,
+                                                       ctx.subtract_mean, cu, ctx.N, fcov, fmean, aux, naux, dqc, dkn,
+                                                       dfc, dfm, want_dlam=need_dl)
+        dl = reduce_lambda_grad(dlam3, lam_t) if need_dl else None
+        if dm0 is not None and not ctx.has_m0:
+            dm0 = None
+        return dq, dk, dl, None, dh0, dm0, None, None, None
+
+
+def fused_ccq_clean_read_l2norm(q, k, lambda_h, *, position_offset=0, initial_cov_state=None,
+                                initial_mean_state=None, output_final_state=False, subtract_mean=True,
+                                cu_seqlens=None):
+    """``q, k = l2norm(q), l2norm(k)`` (fla, eps 1e-6) followed by ``fused_ccq_clean_read`` in one call.
+
+    Takes the raw q and k; returns (q_clean, k_norm, final_cov_state, final_mean_state), where k_norm
+    is the normalised keys the backbone reads next.  Gradients reach the raw q and k (including the
+    gradient the backbone sends back through k_norm).  On the tensor-core path the normalised q
+    never goes to memory: the kernels normalise the tiles they load.
+    """
+    qc, kn, final_cov, final_mean = FusedCCQCleanReadL2Norm.apply(
+        q, k, lambda_h, int(position_offset), initial_cov_state, initial_mean_state,
+        bool(output_final_state), bool(subtract_mean), cu_seqlens,
+    )
+    if not output_final_state:
+        final_cov, final_mean = None, None
+    return qc, kn, final_cov, final_mean
 
 
 class FusedCCQCleanGated(torch.autograd.Function):

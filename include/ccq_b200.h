@@ -87,6 +87,7 @@ size_t ccq_workspace_size(int op, int dtype, int B, int T, int H, int K, int n_s
  * them the exact backward checkpoints a K x K state per chunk).  Same role as ccq_workspace_size.
  */
 #define CCQ_WS_HAVE_FWD_OUTPUTS 1
+#define CCQ_WS_L2NORM 2  /* the call is a ccq_clean_l2norm_* call */
 size_t ccq_workspace_size_for(int op, int dtype, int B, int T, int H, int K, int n_seqs, int flags);
 
 /*
@@ -141,6 +142,52 @@ int ccq_clean_bwd(int dtype, int B, int T, int H, int K,
                   void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
                   float* dinitial_cov, float* dinitial_mean,
                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Forward with the L2 normalisation of q and k inside the operator.  Replaces the pair
+ *   q = l2norm(q, eps=1e-6); k = l2norm(k, eps=1e-6); fused_ccq_clean_read(q, k, ...)
+ * that both fused_chunk orchestrators run (ccq/ops/ccq_gdn/fused_chunk.py:42-53 with
+ * use_qk_l2norm_in_kernel, ccq/ops/ccq_gla/fused_chunk.py:31-41; fla l2norm at
+ * fla/modules/l2norm.py:266): y = x / sqrt(sum(x^2) + 1e-6) per (token, head), fp32 math, rounded to
+ * the activation dtype, then the operator on the normalised q and k.
+ *   q, k: the raw (un-normalised) inputs.
+ *   k_norm: output [B,T,H,K], the normalised keys (the backbone reads them next).
+ *   norm_aux: output [B,T,H,2] f32, per token and head 1/|q| and 1/|k|; the backward reads it.
+ *   Everything else as ccq_clean_fwd.  The tensor-core path normalises the tiles it loads, so the
+ *   normalised q never goes to memory; the exact path keeps it in the workspace
+ *   (ccq_workspace_size_for with CCQ_WS_L2NORM).
+ */
+int ccq_clean_l2norm_fwd(int dtype, int B, int T, int H, int K,
+                         const void* q, const void* k,
+                         int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                         float* token_aux, float* norm_aux,
+                         const int64_t* cu_seqlens, int n_seqs,
+                         int position_offset, int subtract_mean,
+                         const float* initial_cov, const float* initial_mean,
+                         void* q_clean, void* k_norm, float* final_cov, float* final_mean,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of ccq_clean_l2norm_fwd: gradients on the RAW q and k.  Replaces the backward of the same
+ * l2norm + fused_ccq_clean_read pair (fla l2norm_bwd, fla/modules/l2norm.py:49-72, and
+ * FusedCCQCleanRead.backward, fused_read.py:496-514), including autograd's sum of the two
+ * gradients on the normalised keys (the operator's and the backbone's).
+ *   q: the raw queries; k_norm: the forward's k_norm output; norm_aux: the forward's norm_aux.
+ *   dk_norm: optional gradient arriving on k_norm from the rest of the model (NULL = none).
+ *   dq, dk: outputs, gradients on the raw q and k.  Everything else as ccq_clean_bwd.
+ */
+int ccq_clean_l2norm_bwd(int dtype, int B, int T, int H, int K,
+                         const void* q, const void* k_norm,
+                         int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                         const int64_t* cu_seqlens, int n_seqs,
+                         int position_offset, int subtract_mean,
+                         const float* initial_cov, const float* initial_mean,
+                         const float* state_cov, const float* state_mean, const float* token_aux,
+                         const float* norm_aux,
+                         const void* dq_clean, const void* dk_norm, const float* dfinal_cov, const float* dfinal_mean,
+                         void* dq, void* dk, float* dlam, float* dgate_w, float* dgate_b,
+                         float* dinitial_cov, float* dinitial_mean,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Backward that allocates nothing.  No counterpart in the reference: the reference's backward gets

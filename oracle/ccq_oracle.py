@@ -293,3 +293,24 @@ def lambda_dense_bwd(q_pre, W, lam, dlam):
     dW = dpre.reshape(B * T, H).T @ x
     db = dpre.sum(axis=(0, 1))
     return dx.reshape(B, T, H, K), dW, db
+
+
+def l2norm_fwd(x, eps=1e-6, round_to=None):
+    """fla's l2norm (fla/modules/l2norm.py:26-46, :266): y = x / sqrt(sum(x^2) + eps) per row.
+
+    Returns (y, r) with r = 1 / sqrt(sum(x^2) + eps).  ``round_to`` (a callable) rounds y to the
+    activation dtype the way the kernels store it; the backward then uses the rounded y, as fla's
+    saves its stored output."""
+    x = np.asarray(x, np.float64)
+    r = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True) + eps)
+    y = x * r
+    if round_to is not None:
+        y = round_to(y)
+    return y, r[..., 0]
+
+
+def l2norm_bwd(y, r, dy):
+    """fla's l2norm backward (fla/modules/l2norm.py:49-72): dx = r (dy - y sum(dy * y))."""
+    y = np.asarray(y, np.float64)
+    dy = np.asarray(dy, np.float64)
+    return r[..., None] * (dy - y * (dy * y).sum(-1, keepdims=True))

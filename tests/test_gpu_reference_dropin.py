@@ -156,17 +156,27 @@ def test_fused_ccq_clean_read_against_reference(ref, case, dtype):
 # ------------------------------------------------------------------------------------------------
 
 class _Recorder:
-    """Wraps this library's fused_ccq_clean_read to keep the inputs and q_clean of its last call."""
+    """Wraps ops.fused_ccq_clean_read_l2norm (what the B200 orchestrators call) to keep the raw inputs
+    and outputs of its last call."""
 
     def __init__(self):
-        import ccq_b200
-        self.fn = ccq_b200.fused_ccq_clean_read
+        from ccq_b200 import ops
+        self.ops = ops
+        self.fn = ops.fused_ccq_clean_read_l2norm
         self.last = None
 
     def __call__(self, q, k, lambda_h, **kw):
         out = self.fn(q, k, lambda_h, **kw)
-        self.last = (q.detach().clone(), k.detach().clone(), lambda_h.detach().clone(), kw, out[0].detach().clone())
+        self.last = (q.detach().clone(), k.detach().clone(), lambda_h.detach().clone(), kw, out[0].detach().clone(),
+                     out[1].detach().clone())
         return out
+
+    def __enter__(self):
+        self.ops.fused_ccq_clean_read_l2norm = self
+        return self
+
+    def __exit__(self, *exc):
+        self.ops.fused_ccq_clean_read_l2norm = self.fn
 
 
 def _orchestrator_inputs(dtype, B=2, T=200, H=4, K=128, V=64, seed=5):
@@ -195,32 +205,45 @@ def _run_orchestrator(fn, x, dtype, gla):
     return out
 
 
-@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16], ids=['fp32', 'bf16'])
+# bf16 only: the fla backbones these entry points call compile (and autotune) every kernel again
+# per dtype, and their fp32 builds take tens of minutes; the fp32 operator itself is checked above
+@pytest.mark.parametrize('dtype', [torch.bfloat16], ids=['bf16'])
+@pytest.mark.parametrize('attn_mode', ['fused_chunk', 'chunk'])
 @pytest.mark.parametrize('mode', ['gdn', 'gla'])
-def test_fused_chunk_orchestrator_patched_vs_shipped(ref, mode, dtype):
-    """fused_chunk_ccq_gdn (ccq/ops/ccq_gdn/fused_chunk.py:16-59) / fused_chunk_ccq_gla
-    (ccq/ops/ccq_gla/fused_chunk.py:16-46), as the layers call them for attn_mode "fused_chunk"."""
+def test_orchestrator_patched_vs_shipped(ref, mode, attn_mode, dtype):
+    """The layers' attn_mode entry points: fused_chunk_ccq_gdn (ccq/ops/ccq_gdn/fused_chunk.py:16-59),
+    fused_chunk_ccq_gla (ccq/ops/ccq_gla/fused_chunk.py:16-46), chunk_ccq_gdn (ccq/ops/ccq_gdn/chunk.py:11-87)
+    and chunk_ccq_gla (ccq/ops/ccq_gla/chunk.py:17-64), looked up by name in the reference's package as its
+    layers do (ccq/gdn/layer.py:14-18), as shipped and after install()."""
+    import importlib
+
     from ccq_b200 import integration
-    mod = ref['gdn_chunk'] if mode == 'gdn' else ref['gla_chunk']
-    fname = 'fused_chunk_ccq_gdn' if mode == 'gdn' else 'fused_chunk_ccq_gla'
+    pkg = importlib.import_module(f'ccq.ops.ccq_{mode}')
+    fname = f'{attn_mode}_ccq_{mode}'
     x = _orchestrator_inputs(dtype)
-    shipped = _run_orchestrator(getattr(mod, fname), x, dtype, mode == 'gla')
+    shipped = _run_orchestrator(getattr(pkg, fname), x, dtype, mode == 'gla')
     integration.install()
-    rec = _Recorder()
     try:
-        setattr(mod, 'fused_ccq_clean_read', rec)
-        patched = _run_orchestrator(getattr(mod, fname), x, dtype, mode == 'gla')
+        assert getattr(pkg, fname) is getattr(integration, fname)
+        with _Recorder() as rec:
+            patched = _run_orchestrator(getattr(pkg, fname), x, dtype, mode == 'gla')
     finally:
         integration.uninstall()
-    assert rec.last is not None, 'the patched orchestrator did not reach the B200 operator'
-    # the operator's output against the oracle on exactly the (l2-normalised) inputs it received
-    q, k, lam, kw, qc = rec.last
-    oq, _, _ = O.clean_read_fwd(_np(q), _np(k), _np(lam), kw.get('position_offset', 0), None, None, False,
+    assert rec.last is not None, 'the patched orchestrator did not reach the fused l2norm + cleaning operator'
+    # the operator's outputs against the oracle: fla's l2norm then the cleaning, on the raw inputs it got
+    q, k, lam, kw, qc, kn = rec.last
+    rnd = (lambda a: torch.tensor(a).to(dtype).double().numpy())
+    qh, _ = O.l2norm_fwd(_np(q), round_to=rnd)
+    kh, _ = O.l2norm_fwd(_np(k), round_to=rnd)
+    oq, _, _ = O.clean_read_fwd(qh, kh, _np(lam), kw.get('position_offset', 0), None, None, False,
                                 kw.get('subtract_mean', True), None)
-    _check(f'{mode}.q_clean', qc, None, oq, dtype, None)
-    tol = 1e-4 if dtype == torch.float32 else 3e-2
+    _check(f'{mode}.{attn_mode}.k_norm', kn, None, kh, dtype, None)
+    _check(f'{mode}.{attn_mode}.q_clean', qc, None, oq, dtype, None)
+    # chunk mode's reference reads z through fla's chunk_simple_gla (a different summation than its
+    # fused_chunk kernels): a slightly looser bound against it in fp32
+    tol = (1e-4 if attn_mode == 'fused_chunk' else 1e-3) if dtype == torch.float32 else 3e-2
     for name, val in patched.items():
-        _check(f'{mode}.{name}', val, shipped[name], None, dtype, tol)
+        _check(f'{mode}.{attn_mode}.{name}', val, shipped[name], None, dtype, tol)
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16], ids=['fp32', 'bf16'])

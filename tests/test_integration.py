@@ -54,11 +54,18 @@ def test_install_rebinds_and_uninstall_restores(ccq_ref):
         assert gla.fused_ccq_clean_read is ops.fused_ccq_clean_read
         assert gdn_rec.fused_ccq_clean is ops.fused_ccq_clean
         assert gla_rec.fused_recurrent_ccq_gla is integration.fused_recurrent_ccq_gla
+        # the attn_mode orchestrators, in their modules and packages
+        for mod, name in (('ccq.ops.ccq_gdn.fused_chunk', 'fused_chunk_ccq_gdn'), ('ccq.ops.ccq_gdn', 'fused_chunk_ccq_gdn'),
+                          ('ccq.ops.ccq_gdn.chunk', 'chunk_ccq_gdn'), ('ccq.ops.ccq_gdn', 'chunk_ccq_gdn'),
+                          ('ccq.ops.ccq_gla.fused_chunk', 'fused_chunk_ccq_gla'), ('ccq.ops.ccq_gla', 'fused_chunk_ccq_gla'),
+                          ('ccq.ops.ccq_gla.chunk', 'chunk_ccq_gla'), ('ccq.ops.ccq_gla', 'chunk_ccq_gla')):
+            assert getattr(importlib.import_module(mod), name) is getattr(integration, name), (mod, name)
     finally:
         integration.uninstall()
     now = (fr.fused_ccq_clean_read, gdn.fused_ccq_clean_read, gla.fused_ccq_clean_read, gdn_rec.fused_ccq_clean,
            gla_rec.fused_recurrent_ccq_gla)
     assert all(a is b for a, b in zip(orig, now))
+    assert importlib.import_module('ccq.ops.ccq_gdn.fused_chunk').fused_chunk_ccq_gdn is not integration.fused_chunk_ccq_gdn
 
 
 def test_signatures_match_reference(ccq_ref):
@@ -68,8 +75,14 @@ def test_signatures_match_reference(ccq_ref):
     from ccq.ops.ccq_gdn.fused_clean import fused_ccq_clean as ref_clean
     from ccq.ops.ccq_gla.fused_recurrent import fused_recurrent_ccq_gla as ref_gla
     from ccq.ops.common.fused_read import fused_ccq_clean_read as ref_read
+    from ccq.ops.ccq_gdn.chunk import chunk_ccq_gdn as ref_chunk_gdn
+    from ccq.ops.ccq_gdn.fused_chunk import fused_chunk_ccq_gdn as ref_fc_gdn
+    from ccq.ops.ccq_gla.chunk import chunk_ccq_gla as ref_chunk_gla
+    from ccq.ops.ccq_gla.fused_chunk import fused_chunk_ccq_gla as ref_fc_gla
     for ours, ref in ((ops.fused_ccq_clean_read, ref_read), (ops.fused_ccq_clean, ref_clean),
-                      (integration.fused_recurrent_ccq_gla, ref_gla)):
+                      (integration.fused_recurrent_ccq_gla, ref_gla), (integration.fused_chunk_ccq_gdn, ref_fc_gdn),
+                      (integration.fused_chunk_ccq_gla, ref_fc_gla), (integration.chunk_ccq_gdn, ref_chunk_gdn),
+                      (integration.chunk_ccq_gla, ref_chunk_gla)):
         a = inspect.signature(ours).parameters
         b = inspect.signature(ref).parameters
         assert list(a) == list(b), (ours.__name__, list(a), list(b))
