@@ -5,6 +5,7 @@ from .ops import (  # noqa: F401
     FusedCCQCleanReadL2Norm,
     ccq_gate_lambda,
     decode_step,
+    decode_step_l2norm,
     fused_ccq_clean,
     fused_ccq_clean_gated,
     fused_ccq_clean_read,

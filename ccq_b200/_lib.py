@@ -21,7 +21,7 @@ PATHS = {0: 'none', 1: 'simt', 2: 'tcgen05', 3: 'decode'}
 EXPORTS = ('ccq_last_error', 'ccq_last_path', 'ccq_version', 'ccq_last_launch_count',
            'ccq_workspace_size', 'ccq_workspace_size_for', 'ccq_device_status', 'ccq_clean_fwd', 'ccq_clean_bwd',
            'ccq_decode_step', 'ccq_clean_bwd_noalloc', 'ccq_noalloc_status', 'ccq_clean_l2norm_fwd',
-           'ccq_clean_l2norm_bwd')
+           'ccq_clean_l2norm_bwd', 'ccq_decode_step_l2norm')
 CCQ_WS_HAVE_FWD_OUTPUTS, CCQ_WS_L2NORM = 1, 2
 
 _P = ctypes.c_void_p
@@ -44,6 +44,8 @@ _SIGS = {
     'ccq_clean_bwd_noalloc': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P,
                                    _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     'ccq_decode_step': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    'ccq_decode_step_l2norm': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P,
+                                    _P, _P, _P]),
     'ccq_clean_l2norm_fwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P,
                                   _P, _P, _P, _P, _SZ, _P]),
     'ccq_clean_l2norm_bwd': (_I, [_I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P,

@@ -357,6 +357,16 @@ int ccq_decode_step(int dtype, int B, int T, int H, int K, const void* q, const 
                     const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens, int n_seqs,
                     int position_offset, int subtract_mean, const float* cov_in, const float* mean_in,
                     float* cov_out, float* mean_out, void* q_clean, void* stream) {
+  return ccq_decode_step_l2norm(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs,
+                                position_offset, subtract_mean, cov_in, mean_in, cov_out, mean_out, q_clean, nullptr,
+                                stream);
+}
+
+int ccq_decode_step_l2norm(int dtype, int B, int T, int H, int K, const void* q, const void* k, int lambda_mode,
+                           const void* lam, const float* gate_w, const float* gate_b, const int64_t* cu_seqlens,
+                           int n_seqs, int position_offset, int subtract_mean, const float* cov_in,
+                           const float* mean_in, float* cov_out, float* mean_out, void* q_clean, void* k_norm,
+                           void* stream) {
   g_err[0] = 0;
   int st = check_common(dtype, B, T, H, K, q, k, lambda_mode, lam, gate_w, gate_b, cu_seqlens, n_seqs);
   if (st != CCQ_OK) return st;
@@ -372,6 +382,8 @@ int ccq_decode_step(int dtype, int B, int T, int H, int K, const void* q, const 
   a.cov_out = cov_out;
   a.mean_out = mean_out;
   a.q_clean = q_clean;
+  a.qk_norm = k_norm != nullptr;
+  a.k_norm = k_norm;
   int launches = 0;
   cudaError_t e = ccq::decode_step(a, &launches);
   if (e != cudaSuccess) return cuda_fail(e, "ccq_decode_step launch");

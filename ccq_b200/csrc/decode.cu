@@ -21,7 +21,9 @@ namespace {
 constexpr int DT = 256;  // threads per CTA
 
 // VT: state columns per CTA (multiple of 4); NCG = VT / 4 column groups; RG = DT / NCG row groups.
-template <typename Tin, int VT, int KMAX>
+// NORM: q and k arrive raw and are L2-normalised here as fla's l2norm does it (fp32 math, eps 1e-6,
+// rounded to the activation dtype; fla/modules/l2norm.py:26-46), and the normalised k is written out.
+template <typename Tin, int VT, int KMAX, int NORM>
 __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
   constexpr int NCG = VT / 4;
   constexpr int RG = DT / NCG;
@@ -37,7 +39,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
   __shared__ float s_q[KMAX], s_k[KMAX], s_m[KMAX], s_w[KMAX];
   __shared__ float4 s_z[RG][NCG];
   __shared__ float s_red[DT / 32];
-  __shared__ float s_lam, s_s;
+  __shared__ float s_lam, s_s, s_rn[2];
 
   float4 c[RPT];
 #pragma unroll
@@ -58,11 +60,38 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
   for (int t = 0; t < sq.len; ++t) {
     const int64_t row = ((sq.bos + t) * H + h) * (int64_t)K;
     __syncthreads();  // previous token's readers of s_q/s_k/s_m are done
-    for (int i = tid; i < K; i += DT) {
-      const float kv = Act<Tin>::load(kp + row + i);
-      s_q[i] = Act<Tin>::load(q + row + i);
-      s_k[i] = kv;
-      s_m[i] += kv;
+    if (NORM) {
+      for (int i = tid; i < K; i += DT) {
+        s_q[i] = Act<Tin>::load(q + row + i);
+        s_k[i] = Act<Tin>::load(kp + row + i);
+      }
+      __syncthreads();
+      if (warp < 2) {
+        const float* x = warp == 0 ? s_q : s_k;
+        float ss = 0.f;
+        for (int i = lane; i < K; i += 32) ss = fmaf(x[i], x[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) s_rn[warp] = 1.0f / sqrtf(ss + 1e-6f);
+      }
+      __syncthreads();
+      const float rq = s_rn[0], rk = s_rn[1];
+      for (int i = tid; i < K; i += DT) {
+        Tin qh, kh;
+        Act<Tin>::store(&qh, s_q[i] * rq);
+        Act<Tin>::store(&kh, s_k[i] * rk);
+        const float kv = Act<Tin>::load(&kh);
+        s_q[i] = Act<Tin>::load(&qh);
+        s_k[i] = kv;
+        s_m[i] += kv;
+        if (vt == 0) reinterpret_cast<Tin*>(a.k_norm)[row + i] = kh;
+      }
+    } else {
+      for (int i = tid; i < K; i += DT) {
+        const float kv = Act<Tin>::load(kp + row + i);
+        s_q[i] = Act<Tin>::load(q + row + i);
+        s_k[i] = kv;
+        s_m[i] += kv;
+      }
     }
     __syncthreads();
     // s = m_t . q_t and (GATE) the lambda pre-activation, one warp each
@@ -140,7 +169,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(CleanArgs a) {
 }
 
 // one launch; the column tiles of a (document, head) run as one cluster (gridDim.x CTAs, <= 8)
-template <typename Tin, int VT, int KMAX>
+template <typename Tin, int VT, int KMAX, int NORM>
 cudaError_t launch_tiles(const CleanArgs& a) {
   const unsigned tiles = (unsigned)((a.K + VT - 1) / VT);
   cudaLaunchConfig_t cfg = {};
@@ -155,15 +184,19 @@ cudaError_t launch_tiles(const CleanArgs& a) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = tiles > 1 ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, decode_kernel<Tin, VT, KMAX>, a);
+  return cudaLaunchKernelEx(&cfg, decode_kernel<Tin, VT, KMAX, NORM>, a);
+}
+
+template <typename Tin, int NORM>
+cudaError_t launch_norm(const CleanArgs& a) {
+  if (a.K <= 64) return launch_tiles<Tin, 64, 64, NORM>(a);
+  if (a.K <= 128) return launch_tiles<Tin, 128, 128, NORM>(a);
+  return launch_tiles<Tin, 64, 256, NORM>(a);
 }
 
 template <typename Tin>
 cudaError_t launch(const CleanArgs& a, int* launches) {
-  cudaError_t e;
-  if (a.K <= 64) e = launch_tiles<Tin, 64, 64>(a);
-  else if (a.K <= 128) e = launch_tiles<Tin, 128, 128>(a);
-  else e = launch_tiles<Tin, 64, 256>(a);
+  cudaError_t e = a.qk_norm ? launch_norm<Tin, 1>(a) : launch_norm<Tin, 0>(a);
   *launches += 1;
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

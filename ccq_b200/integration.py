@@ -51,13 +51,11 @@ def fused_recurrent_ccq_gla(q, k, v, lambda_h, gk=None, gv=None, scale=None, ini
     Same arguments and returns: (o, final_state, final_cov_state, final_mean_state).
     """
     from fla.ops.gla.fused_recurrent import fused_recurrent_gla
-    q = ops.l2norm(q, eps=1e-6)
-    k = ops.l2norm(k, eps=1e-6)
-    q_clean, _, final_cov_state, final_mean_state, _ = ops.fused_ccq_clean(
+    q_clean, k, final_cov_state, final_mean_state, _ = ops.fused_ccq_clean(
         q, k, lambda_h, initial_cov_state=initial_cov_state,
         initial_mean_state=initial_mean_state if subtract_mean else None,
-        output_final_state=output_final_state, cu_seqlens=cu_seqlens, position_offset=position_offset,
-        subtract_mean=subtract_mean, use_chunk=False)
+        output_final_state=output_final_state, cu_seqlens=cu_seqlens, use_qk_l2norm_in_kernel=True,
+        position_offset=position_offset, subtract_mean=subtract_mean, use_chunk=False)
     o, final_state = fused_recurrent_gla(q=q_clean, k=k, v=v, gk=gk, gv=gv, scale=scale,
                                          initial_state=initial_state, output_final_state=output_final_state,
                                          reverse=reverse, cu_seqlens=cu_seqlens)

@@ -430,6 +430,22 @@ def decode_step(q, k, lambda_h, cov_state=None, mean_state=None, *, position_off
     Returns (q_clean, cov_state_after [N,H,K,K] fp32, mean_state_after [N,H,K] fp32 or None).
     ``inplace=True`` updates the given cache tensors instead of allocating new ones.
     """
+    qc, _, cov, mean = _decode(q, k, lambda_h, cov_state, mean_state, position_offset, subtract_mean, cu_seqlens,
+                               gate_w, gate_b, inplace, False)
+    return qc, cov, mean
+
+
+def decode_step_l2norm(q, k, lambda_h, cov_state=None, mean_state=None, *, position_offset=0, subtract_mean=True,
+                       cu_seqlens=None, gate_w=None, gate_b=None, inplace=False):
+    """decode_step on RAW q and k, with fla's l2norm of both (eps 1e-6) done inside the kernel.
+
+    Returns (q_clean, k_norm, cov_state_after, mean_state_after); k_norm is what the backbone reads."""
+    return _decode(q, k, lambda_h, cov_state, mean_state, position_offset, subtract_mean, cu_seqlens, gate_w, gate_b,
+                   inplace, True)
+
+
+def _decode(q, k, lambda_h, cov_state, mean_state, position_offset, subtract_mean, cu_seqlens, gate_w, gate_b,
+            inplace, l2norm_qk):
     _check_cuda(q, k, lambda_h if isinstance(lambda_h, torch.Tensor) else None, cov_state, mean_state,
                 cu_seqlens, gate_w, gate_b)
     q = q.detach().contiguous()
@@ -464,13 +480,14 @@ def decode_step(q, k, lambda_h, cov_state=None, mean_state=None, *, position_off
     W = gate_w.detach().float().contiguous() if gate else None
     bb = gate_b.detach().float().contiguous() if gate else None
     mode = _lib.CCQ_LAMBDA_GATE if gate else _lib.CCQ_LAMBDA_TOKEN
+    kn = torch.empty_like(k) if l2norm_qk else None
     lib = _lib.load()
     with torch.cuda.device(dev):
-        st = lib.ccq_decode_step(_dtype_code(q), B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(W), _p(bb), _p(cu), N,
-                                 int(position_offset), int(bool(subtract_mean)), _p(cov_in), _p(mean_in),
-                                 _p(cov_out), _p(mean_out), _p(qc), _stream(dev))
+        st = lib.ccq_decode_step_l2norm(_dtype_code(q), B, T, H, K, _p(q), _p(k), mode, _p(lam3), _p(W), _p(bb), _p(cu),
+                                        N, int(position_offset), int(bool(subtract_mean)), _p(cov_in), _p(mean_in),
+                                        _p(cov_out), _p(mean_out), _p(qc), _p(kn), _stream(dev))
     _lib.check(st)
-    return qc, cov_out, mean_out
+    return qc, kn, cov_out, mean_out
 
 
 def l2norm(x, eps=1e-6):
@@ -486,24 +503,30 @@ def fused_ccq_clean(q, k, lambda_h, *, initial_cov_state=None, initial_mean_stat
 
     Returns (q_clean, k, final_cov_state, final_mean_state, use_qk_l2norm_in_kernel).  Inference
     calls run the decode kernel; calls that need gradients run the chunked operator, whose math
-    is identical (the inclusive read z_t = C_t q_t at pos_t = t + 1 + position_offset).
+    is identical (the inclusive read z_t = C_t q_t at pos_t = t + 1 + position_offset).  With
+    ``use_qk_l2norm_in_kernel`` the normalisation of q and k happens inside those kernels and the
+    returned k is the normalised one (as the reference returns it), with the flag cleared.
     """
-    if use_qk_l2norm_in_kernel:
-        q = l2norm(q, eps=1e-6)
-        k = l2norm(k, eps=1e-6)
-        use_qk_l2norm_in_kernel = False
+    norm = bool(use_qk_l2norm_in_kernel)
     needs_grad = torch.is_grad_enabled() and any(
         isinstance(t, torch.Tensor) and t.requires_grad
         for t in (q, k, lambda_h, initial_cov_state, initial_mean_state))
+    m0 = initial_mean_state if subtract_mean else None
     if needs_grad or (use_chunk and q.shape[1] > chunk_size):
-        qc, fc, fm = fused_ccq_clean_read(q, k, lambda_h, position_offset=position_offset,
-                                          initial_cov_state=initial_cov_state,
-                                          initial_mean_state=initial_mean_state if subtract_mean else None,
-                                          output_final_state=output_final_state, subtract_mean=subtract_mean,
-                                          cu_seqlens=cu_seqlens)
-        return qc, k, fc, fm, use_qk_l2norm_in_kernel
-    qc, fc, fm = decode_step(q, k, lambda_h, initial_cov_state, initial_mean_state, position_offset=position_offset,
-                             subtract_mean=subtract_mean, cu_seqlens=cu_seqlens)
+        kw = dict(position_offset=position_offset, initial_cov_state=initial_cov_state, initial_mean_state=m0,
+                  output_final_state=output_final_state, subtract_mean=subtract_mean, cu_seqlens=cu_seqlens)
+        if norm:
+            qc, k, fc, fm = fused_ccq_clean_read_l2norm(q, k, lambda_h, **kw)
+        else:
+            qc, fc, fm = fused_ccq_clean_read(q, k, lambda_h, **kw)
+        return qc, k, fc, fm, False
+    if norm:
+        qc, k, fc, fm = decode_step_l2norm(q, k, lambda_h, initial_cov_state, initial_mean_state,
+                                           position_offset=position_offset, subtract_mean=subtract_mean,
+                                           cu_seqlens=cu_seqlens)
+    else:
+        qc, fc, fm = decode_step(q, k, lambda_h, initial_cov_state, initial_mean_state,
+                                 position_offset=position_offset, subtract_mean=subtract_mean, cu_seqlens=cu_seqlens)
     if not output_final_state:
         fc, fm = None, None
-    return qc, k, fc, fm, use_qk_l2norm_in_kernel
+    return qc, k, fc, fm, False

@@ -249,6 +249,24 @@ int ccq_decode_step(int dtype, int B, int T, int H, int K,
                     float* cov_out, float* mean_out,
                     void* q_clean, void* stream);
 
+/*
+ * The decode step with the L2 normalisation of q and k inside the kernel.  Replaces
+ *   fused_ccq_clean(q, k, ..., use_qk_l2norm_in_kernel=True, use_chunk=False)
+ * (ccq/ops/ccq_gdn/fused_clean.py:34-83: fla l2norm of both, then the recurrent read and the
+ * cleaning), which the GDN layer's fused_recurrent mode calls (ccq/gdn/layer.py:374-390), and the
+ * l2norm + cleaning sequence of ccq/ops/ccq_gla/fused_recurrent.py:26-38.
+ *   q, k: the raw tokens; k_norm: output [B,T,H,K], the normalised keys (what the cache and the
+ *   backbone see); everything else as ccq_decode_step.  With k_norm == NULL this is ccq_decode_step.
+ */
+int ccq_decode_step_l2norm(int dtype, int B, int T, int H, int K,
+                           const void* q, const void* k,
+                           int lambda_mode, const void* lam, const float* gate_w, const float* gate_b,
+                           const int64_t* cu_seqlens, int n_seqs,
+                           int position_offset, int subtract_mean,
+                           const float* cov_in, const float* mean_in,
+                           float* cov_out, float* mean_out,
+                           void* q_clean, void* k_norm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

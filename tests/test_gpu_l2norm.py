@@ -128,3 +128,33 @@ def test_l2norm_tcgen05_matches_exact_path(case, monkeypatch):
         e = (out[name].float() - ref[name].float()).abs().max().item()
         assert e <= 2e-2, (name, e)
     assert torch.equal(out['k_norm'], ref['k_norm']) or (out['k_norm'].float() - ref['k_norm'].float()).abs().max() <= 8e-3
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16], ids=['fp32', 'bf16'])
+@pytest.mark.parametrize('K', [64, 128, 256])
+def test_decode_l2norm_against_oracle(dtype, K):
+    """decode_step_l2norm (ccq_decode_step_l2norm): raw q, k of a few tokens normalised in the decode
+    kernel, on a cache built from a prefix; the cache update uses the normalised keys."""
+    import ccq_b200
+    g = torch.Generator(device='cuda').manual_seed(21)
+    N, H, T, P = 3, 2, 2, 30
+    kk = torch.nn.functional.normalize(torch.randn(N, P, H, K, generator=g, device='cuda'), dim=-1)
+    C0 = torch.einsum('nthk,nthv->nhkv', kk, kk)
+    m0 = kk.sum(1)
+    q = (torch.randn(N, T, H, K, generator=g, device='cuda') * 3).to(dtype)
+    k = (torch.randn(N, T, H, K, generator=g, device='cuda') * 3).to(dtype)
+    lam = torch.rand(N, T, H, generator=g, device='cuda').to(dtype)
+    qc, kn, C1, m1 = ccq_b200.decode_step_l2norm(q, k, lam, C0, m0, position_offset=P)
+    assert ccq_b200.last_path() == 'decode'
+    rnd = (lambda a: torch.tensor(a).to(dtype).double().numpy())
+    qh, _ = O.l2norm_fwd(_np(q), round_to=rnd)
+    kh, _ = O.l2norm_fwd(_np(k), round_to=rnd)
+    oq, oC, om = O.decode_clean(qh, kh, _np(lam), P, _np(C0), _np(m0))
+    if dtype == torch.float32:
+        assert rel_err(_np(qc), oq) <= 1e-5
+        assert rel_err(_np(kn), kh) <= 1e-6
+    else:
+        assert np.abs(_np(qc) - oq).max() <= 2e-2
+        assert np.abs(_np(kn) - kh).max() <= 8e-3
+    assert rel_err(_np(C1), oC) <= 1e-5
+    assert rel_err(_np(m1), om) <= 1e-5
