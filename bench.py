@@ -56,7 +56,9 @@ def parse():
     ap.add_argument('--steps', type=int, default=50)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='all', choices=['all', 'c2', 'c3', 'c4', 'c5'])
+    ap.add_argument('--workload', default='all', choices=['all', 'c2', 'c2_l2norm', 'c3', 'c4', 'c5'])
+    ap.add_argument('--batch', type=int, default=8,
+                    help='batch rows per GPU of c2 / c2_l2norm (8 is the benchmark; smaller for profiling)')
     ap.add_argument('--e2e-steps', type=int, default=10)
     ap.add_argument('--soak-s', type=float, default=1.5,
                     help='seconds of untimed c2 steps run under the clock sampler before the timed steps')
@@ -162,10 +164,10 @@ def c3_lengths(seed, n_docs=32, lo=128, hi=8192):
 
 def c2_config(world, B=8, T=4096, H=16, K=128):
     """The c2 workload description shared by both arms of the bench."""
-    return {'workload': 'c2: B=8/GPU,T=4096,H=16,d_k=128 cleaning fwd+bwd, per-head gate fused',
+    return {'workload': f'c2: B={B}/GPU,T={T},H={H},d_k={K} cleaning fwd+bwd, per-head gate fused',
             'global_batch': B * world, 'seq_len': T, 'heads': H, 'd_k': K,
             'parallelism': f'dp{world} (batch shards, NCCL all-reduce of dW,db)',
-            'l2': 'inputs larger than L2 (q,k,dq_clean 384 MiB per GPU)'}
+            'l2': f'inputs larger than L2 (q,k,dq_clean {3 * B * T * H * K * 2 >> 20} MiB per GPU)'}
 
 
 def roofline_of(th, step_s, hbm_peak, tf_peak):
@@ -281,8 +283,8 @@ def run_c2(args, rank, world, device, hbm_peak, tf_peak, peak_kind, reducer):
     import ccq_b200
     from ccq_b200 import _lib, ops
 
-    B, T, H, K = 8, 4096, 16, 128
-    q, k, W, bias, dqc = c2_inputs(device, 1000 + rank)
+    B, T, H, K = args.batch, 4096, 16, 128
+    q, k, W, bias, dqc = c2_inputs(device, 1000 + rank, B=B)
     stream = torch.cuda.current_stream(device)
     launches = [0]
 
@@ -535,7 +537,7 @@ def run_c2_l2norm(args, rank, world, device, hbm_peak, tf_peak):
     import torch
 
     import ccq_b200
-    B, T, H, K = 8, 4096, 16, 128
+    B, T, H, K = args.batch, 4096, 16, 128
     gen = torch.Generator(device=device).manual_seed(1500 + rank)
     q0 = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
     k0 = torch.randn(B, T, H, K, generator=gen, device=device).to(torch.bfloat16)
@@ -631,15 +633,24 @@ def run_triton_reference(args, device):
             for _ in range(max(3, args.warmup)):
                 o = step()
             torch.cuda.synchronize(device)
-            outs[name] = [t.float() for t in o]
+            outs[name] = [None if t is None else t.float() for t in o]
             el, _ = timed_steps(step, args.steps, stream)
+            # forward alone, same call
+            q = q0.detach().requires_grad_(True)
+            k = k0.detach().requires_grad_(True)
+            lam = lam0.detach().requires_grad_(True)
+            ef, _ = timed_steps(lambda: fn(q, k, lam), args.steps, stream)
         except Exception as exc:
             res[name] = {'error': f'{type(exc).__name__}: {exc}'[:300]}
             continue
-        res[name] = {'ms_per_step': el / args.steps * 1e3, 'tokens_per_s': B * T * args.steps / el}
+        res[name] = {'ms_per_step': el / args.steps * 1e3, 'fwd_ms': ef / args.steps * 1e3,
+                     'tokens_per_s': B * T * args.steps / el}
+        if name == 'ours':
+            res[name]['path'] = ccq_b200.last_path()
     if 'reference_triton' in outs and 'ours' in outs:
         res['max_abs_diff'] = {n: float((a - b).abs().max()) for n, a, b in
-                               zip(('q_clean', 'dq', 'dk', 'dlam'), outs['ours'], outs['reference_triton'])}
+                               zip(('q_clean', 'dq', 'dk', 'dlam'), outs['ours'], outs['reference_triton'])
+                               if a is not None and b is not None}
     if 'ms_per_step' in res.get('reference_triton', {}) and 'ms_per_step' in res.get('ours', {}):
         res['speedup'] = res['reference_triton']['ms_per_step'] / res['ours']['ms_per_step']
     res['workload'] = ('c2 (B=8, T=4096, H=16, d_k=128, bf16) fwd+bwd through fused_ccq_clean_read(q, k, lambda) '
@@ -663,7 +674,7 @@ def run_ours(args, rank, world, local_rank):
     try:
         if args.workload in ('all', 'c2'):
             main = run_c2(args, rank, world, device, hbm_peak, tf_peak, peak_kind, reducer)
-        if args.workload in ('all', 'c2'):
+        if args.workload in ('all', 'c2', 'c2_l2norm'):
             extra['c2_l2norm'] = run_c2_l2norm(args, rank, world, device, hbm_peak, tf_peak)
         if args.workload in ('all', 'c3'):
             extra['c3'] = run_c3(args, rank, world, device, hbm_peak, tf_peak)
@@ -693,6 +704,13 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         return
+    if args.workload == 'c2_l2norm':
+        w = extra['c2_l2norm']
+        print(json.dumps({'metric': 'CCQ c2_l2norm tokens/s', 'n_gpus': world, 'steps': args.steps,
+                          'warmup': args.warmup, 'higher_is_better': True, 'dtype': 'bf16', 'data': DATA,
+                          'config': {'workload': w['workload'], 'batch_per_gpu': args.batch}, 'c2_l2norm': w}),
+              flush=True)
+        return
     if args.workload not in ('all', 'c2'):
         # a single extra workload as the line's headline
         w = extra[args.workload]
@@ -708,7 +726,7 @@ def run_ours(args, rank, world, local_rank):
         'value': main['value'], 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
         'ms_per_step': main['ms_per_step'], 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
         'dtype': 'bf16', 'data': DATA,
-        'config': c2_config(world),
+        'config': c2_config(world, B=args.batch),
         'paths': main['paths'],
         'roofline': main['roofline'],
         'clocks': main['clocks'],

@@ -87,6 +87,44 @@ __global__ void __launch_bounds__(32 * NW) l2norm_bwd_kernel(Tin* d, const Tin* 
   }
 }
 
+// 16-bit rows of K = 128: sixteen lanes per row, eight elements (16 bytes) per lane and tensor, two
+// rows per warp; the same arithmetic as l2norm_bwd_kernel.
+template <typename Tin>
+__global__ void __launch_bounds__(32 * NW) l2norm_bwd128_kernel(Tin* d, const Tin* d_ext, const Tin* y,
+                                                              const float* r_in, int slot, int64_t rows) {
+  const int lane = threadIdx.x & 31, sub = lane & 15;
+  const int64_t row = ((int64_t)blockIdx.x * NW + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const bool ok = row < rows;
+  const int64_t off = (ok ? row : 0) * 128 + sub * 8;
+  float s[8], yv[8];
+  uint4 dv = make_uint4(0, 0, 0, 0), ev = make_uint4(0, 0, 0, 0), yy = make_uint4(0, 0, 0, 0);
+  if (ok) {
+    dv = *reinterpret_cast<const uint4*>(d + off);
+    yy = *reinterpret_cast<const uint4*>(y + off);
+    if (d_ext) ev = *reinterpret_cast<const uint4*>(d_ext + off);
+  }
+  const Tin* dp = reinterpret_cast<const Tin*>(&dv);
+  const Tin* ep = reinterpret_cast<const Tin*>(&ev);
+  const Tin* yp = reinterpret_cast<const Tin*>(&yy);
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    s[i] = Act<Tin>::load(dp + i);
+    if (d_ext) s[i] = rnd<Tin>(s[i] + Act<Tin>::load(ep + i));
+    yv[i] = Act<Tin>::load(yp + i);
+    dot = fmaf(s[i], yv[i], dot);
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  if (!ok) return;
+  const float r = r_in[2 * row + slot];
+  uint4 out;
+  Tin* op = reinterpret_cast<Tin*>(&out);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) Act<Tin>::store(op + i, r * (s[i] - yv[i] * dot));
+  *reinterpret_cast<uint4*>(d + off) = out;
+}
+
 template <typename Tin>
 cudaError_t launch_fwd(const void* x, void* y, float* r_out, int slot, int64_t rows, int K, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
@@ -105,6 +143,13 @@ template <typename Tin>
 cudaError_t launch_bwd(void* d, const void* d_ext, const void* y, const float* r_in, int slot, int64_t rows, int K,
                        cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  const bool vec = sizeof(Tin) == 2 && K == 128 && ((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(y) |
+                                                     reinterpret_cast<uintptr_t>(d_ext)) & 15) == 0;
+  if (vec) {
+    const unsigned grid = (unsigned)((rows + 2 * NW - 1) / (2 * NW));
+    l2norm_bwd128_kernel<Tin><<<grid, 32 * NW, 0, st>>>((Tin*)d, (const Tin*)d_ext, (const Tin*)y, r_in, slot, rows);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((rows + NW - 1) / NW);
   l2norm_bwd_kernel<Tin><<<grid, 32 * NW, 0, st>>>((Tin*)d, (const Tin*)d_ext, (const Tin*)y, r_in, slot, rows, K);
   return cudaGetLastError();

@@ -7,7 +7,10 @@ ops.clean_fwd_raw / ops.clean_bwd_raw as the benchmark calls them.  Checked:
     token side outputs, dq, dk, dW, db);
   * three heads across all eight batch rows against the float64 oracle on the same bf16-rounded
     inputs, including the gate gradients dW[h], db[h] summed over the batch.
-Bars: 2e-2 max-abs on bf16 outputs, 1e-5 relative on fp32 states, 1e-2 relative on dW / db.
+Bars: 2e-2 max-abs on bf16 outputs against the oracle (each path); between the two paths 4e-2, as
+each is within 2e-2 of the exact result (dq reaches ~8 here, where one bf16 ulp is 0.031); 1e-4
+relative on the fp32 states (sums of 4096 outer products: the tensor core's fp32 accumulation of
+bf16 products differs from a float64 sum by ~1.3e-5 relative at this length); 1e-2 relative on dW / db.
 """
 import numpy as np
 import pytest
@@ -59,17 +62,21 @@ def test_c2_tcgen05_matches_exact_path(c2, monkeypatch):
     monkeypatch.delenv('CCQ_B200_FORCE_SIMT')
     for name in ('qc', 'dq', 'dk'):
         err = (tc[name].float() - ex[name].float()).abs().max().item()
-        assert err <= BF16_TOL, (name, err)
+        assert err <= 2 * BF16_TOL, (name, err)
     for name in ('fc', 'fm'):
-        assert rel_err(_np(tc[name]), _np(ex[name])) <= 1e-5, name
+        assert rel_err(_np(tc[name]), _np(ex[name])) <= 1e-4, name
     assert rel_err(_np(tc['aux']), _np(ex['aux'])) <= 1e-3
     for name in ('dW', 'db'):
         assert rel_err(_np(tc[name]), _np(ex[name])) <= 1e-2, (name, rel_err(_np(tc[name]), _np(ex[name])))
 
 
+@pytest.mark.parametrize('path', ['tcgen05', 'simt'])
 @pytest.mark.parametrize('h', [0, 7, 15])
-def test_c2_heads_against_oracle(c2, h):
-    tc, _ = _run(c2)
+def test_c2_heads_against_oracle(c2, h, path, monkeypatch):
+    if path == 'simt':
+        monkeypatch.setenv('CCQ_B200_FORCE_SIMT', '1')
+    tc, paths = _run(c2)
+    assert paths == (path, path)
     q, k, W, b, dqc = c2
     qn, kn, gn = (_np(t[:, :, h:h + 1]) for t in (q, k, dqc))
     Wn, bn = _np(W[h:h + 1]), _np(b[h:h + 1])
@@ -80,7 +87,7 @@ def test_c2_heads_against_oracle(c2, h):
     assert np.abs(_np(tc['qc'][:, :, h:h + 1]) - oq).max() <= BF16_TOL
     assert np.abs(_np(tc['dq'][:, :, h:h + 1]) - (odq + dqx)).max() <= BF16_TOL
     assert np.abs(_np(tc['dk'][:, :, h:h + 1]) - odk).max() <= BF16_TOL
-    assert rel_err(_np(tc['fc'][:, h:h + 1]), ofc) <= 1e-5
-    assert rel_err(_np(tc['fm'][:, h:h + 1]), ofm) <= 1e-5
+    assert rel_err(_np(tc['fc'][:, h:h + 1]), ofc) <= 1e-4
+    assert rel_err(_np(tc['fm'][:, h:h + 1]), ofm) <= 1e-4
     assert rel_err(_np(tc['dW'][h:h + 1]), odW) <= 1e-2
     assert rel_err(_np(tc['db'][h:h + 1]), odb) <= 1e-2
