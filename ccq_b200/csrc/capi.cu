@@ -51,7 +51,12 @@ int checked_finish(const char* what, const void* ws, cudaStream_t stream) {
   if (st != CCQ_OK) return st;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, what);
-  if (code != 0) return fail(CCQ_ERR_CUDA, "%s: device pipeline timeout, code %#x", what, code);
+  if (code != 0) {
+    // the words after the code may hold where the pipeline stood (kernel-specific detail)
+    int detail = 0;
+    read_device_word(reinterpret_cast<const int*>(ws) + 1, stream, &detail);
+    return fail(CCQ_ERR_CUDA, "%s: device pipeline timeout, code %#x (detail %#x)", what, code, detail);
+  }
   return CCQ_OK;
 }
 

@@ -32,11 +32,16 @@
 //
 // NORM = 1 (the *_l2norm entry points) takes raw q and k and applies fla's l2norm (y = x / sqrt(|x|^2
 // + 1e-6), fp32 math, rounded to the activation dtype; fla/modules/l2norm.py:26-46) inside the
-// kernel: the aux warps normalise each chunk's Q and K tiles in place in shared memory before the
-// first MMA reads them, write the normalised keys out (TMA bulk store of the K tile; the backbone
-// reads them next) and the two reciprocal norms per token; the output group renormalises the q it
-// re-reads for q_clean with the same factor, so q_clean = q_hat - (lambda / pos) Z exactly as the
-// reference computes it on l2norm's output.
+// kernel.  K: the aux warps normalise each chunk's K tile in place in shared memory before the first
+// MMA reads it (the state update and the masked read need the normalised keys as MMA operands), write
+// it out as k_norm with one TMA bulk store (the backbone reads it next) and record 1/|k|.  Q is never
+// rewritten: with r_t = 1/|q_t| every quantity the kernel forms from q scales by r_t, so the MMAs run
+// on the raw Q tile and r_t is applied where it matters: the scores A_t, the mean-term scalar s_t and
+// the per-token P' row enter the masked read in raw units (P'' = A_raw - s_raw / pos, whose product
+// with r_t is P'), so Z accumulates Z_true / r_t; the gate logit and the token_aux side output take
+// r_t explicitly, and the output group forms q_clean = q_hat - (lambda / pos) r_t Z with q_hat the
+// re-read q rounded after scaling by r_t, as l2norm's output is.  The score group computes r_t from
+// the Q tile (each thread reads its token's full row).
 #include <stdlib.h>
 
 #include "args.h"
@@ -69,7 +74,7 @@ struct FwdSmall {
   float xs[2][2][128];     // [chunk parity][column half][row]: partial s_t
   float cf[2][128];        // [chunk parity][row]: lambda_t / pos_t
   float msum[4][128];      // aux: per token-quarter partial key sums
-  float rn[2][2][128];     // NORM: [stage][q | k][row] reciprocal norms of the stage's chunk
+  float rk[2][128];        // NORM: [stage][row] 1/|k| of the stage's chunk
   float rqo[2][128];       // NORM: [chunk parity][row] 1/|q| handed from the score to the output group
   uint64_t full[2], kready[2], empty[2], a_full[2], a_free[2], cf_ready[2], z_full[2], z_free[2];
   uint64_t c_full, c_read, cprev_free, cconv, pready, qo_full, mma_done;
@@ -303,6 +308,8 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         if (!issued && clock64() - idle0 > (1ll << 31)) {
           *ab = 1;
           atomicOr(err, 2);
+          // detail word: how far each MMA group got (chunk counts of F1, F2a, F3, F2b)
+          atomicExch(err + 1, (min(i1, 255) << 24) | (min(i2a, 255) << 16) | (min(i3, 255) << 8) | min(i2b, 255));
           break;
         }
       }
@@ -343,45 +350,62 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       const uint32_t kt = sbase + F_OFF_K + s * F_KTILE;
       const int valid = min(F_BT, sq.len - c * F_BT);
       if (NORM) {
-        // the chunk's 128 q rows, then its 128 k rows, normalised in place: four threads per row
-        // (16-byte chunks 4 sub .. 4 sub + 3 of the row's 16), 16 rows per pass
-        const uint32_t qt = sbase + F_OFF_Q + s * F_QTILE;
+        // the chunk's 128 k rows normalised in place: four threads per row (16-byte chunks
+        // 4 sub .. 4 sub + 3 of the row's 16), 16 rows per pass, two passes at a time so their
+        // shared-memory loads and reductions overlap (two warps have little else to hide latency
+        // with; more at a time spills registers).  1/sqrt is the hardware reciprocal square root:
+        // the products are rounded to 16 bits, which absorbs its last-bit difference.
         const int sub = at & 3;
         const uint32_t pan = sub >> 1, cc0 = (sub & 1) * 4;
-        for (int pass = 0; pass < 16; ++pass) {
-          const int rr = pass * 16 + (at >> 2);
-          const int isk = rr >= 128;
-          const int row = rr & 127;
-          const uint32_t base = isk ? kt + pan * F_KPANEL : qt + pan * F_QPANEL;
-          uint4 w[4];
-          float ss = 0.f;
+        const uint32_t base = kt + pan * F_KPANEL;
+#pragma unroll 1
+        for (int grp = 0; grp < 8; ++grp) {
+          uint4 w[1][4];
+          float ss[1];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            w[i] = ld_shared_v4(base + sw128(row, cc0 + i));
-            const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+          for (int r4 = 0; r4 < 1; ++r4) {
+            const int row = (grp + r4) * 16 + (at >> 2);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack2<AB16>(u[j]);
-              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-            }
+            for (int i = 0; i < 4; ++i) w[r4][i] = ld_shared_v4(base + sw128(row, cc0 + i));
           }
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-          const float rinv = 1.0f / sqrtf(ss + 1e-6f);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-            uint32_t o[4];
+          for (int r4 = 0; r4 < 1; ++r4) {
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = unpack2<AB16>(u[j]);
-              o[j] = pack2<AB16>(f.x * rinv, f.y * rinv);
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t u[4] = {w[r4][i].x, w[r4][i].y, w[r4][i].z, w[r4][i].w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<AB16>(u[j]);
+                a0 = fmaf(f.x, f.x, a0);
+                a1 = fmaf(f.y, f.y, a1);
+              }
             }
-            st_shared_v4(base + sw128(row, cc0 + i), o[0], o[1], o[2], o[3]);
+            ss[r4] = a0 + a1;
           }
-          if (sub == 0) S.rn[s][isk][row] = rinv;
+#pragma unroll
+          for (int r4 = 0; r4 < 1; ++r4) ss[r4] += __shfl_xor_sync(0xffffffffu, ss[r4], 1);
+#pragma unroll
+          for (int r4 = 0; r4 < 1; ++r4) ss[r4] += __shfl_xor_sync(0xffffffffu, ss[r4], 2);
+#pragma unroll
+          for (int r4 = 0; r4 < 1; ++r4) {
+            const int row = (grp + r4) * 16 + (at >> 2);
+            const float rinv = rsqrtf(ss[r4] + 1e-6f);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t u[4] = {w[r4][i].x, w[r4][i].y, w[r4][i].z, w[r4][i].w};
+              uint32_t o[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<AB16>(u[j]);
+                o[j] = pack2<AB16>(f.x * rinv, f.y * rinv);
+              }
+              st_shared_v4(base + sw128(row, cc0 + i), o[0], o[1], o[2], o[3]);
+            }
+            if (sub == 0) S.rk[s][row] = rinv;
+          }
         }
-        fence_async_smem();  // normalised tiles -> the MMAs and the bulk store
+        fence_async_smem();  // the normalised K tile -> the MMAs and the bulk store
         bar_sync<2, 64>();
         const int t0 = c * F_BT;
         if (valid == F_BT) {
@@ -399,9 +423,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
                 val;
           }
         }
-        for (int t = at; t < valid; t += 64)
-          *reinterpret_cast<float2*>(a.norm_aux + ((sq.bos + t0 + t) * H + h) * 2) =
-              make_float2(S.rn[s][0][t], S.rn[s][1][t]);
+        for (int t = at; t < valid; t += 64) a.norm_aux[((sq.bos + t0 + t) * H + h) * 2 + 1] = S.rk[s][t];
       }
       if (valid < F_BT) {  // keys past the end of the document belong to the next one: zero them
         const uint32_t wp = at >> 5, wi = at & 31;
@@ -473,8 +495,25 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       const int valid = min(F_BT, sq.len - t0);
       pipe_wait(&S.a_full[pb], (c >> 1) & 1, ab, err, 16);
       tc_fence_after();
-      // NORM: 1/|q_t| of this chunk, read while the stage still holds it (it is reloaded after F2b)
-      const float rqv = NORM ? S.rn[pb][0][t] : 1.f;
+      float rqv = 1.f;
+      if (NORM) {
+        // 1/|q_t| from row t of the raw Q tile (the stage holds chunk c until F2b, which waits for
+        // this group); both column halves, so no exchange between the warps of a lane quadrant
+        const uint32_t qrow = sbase + F_OFF_Q + pb * F_QTILE;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          const uint4 w4 = ld_shared_v4(qrow + (cc >> 3) * F_QPANEL + sw128(t, cc & 7));
+          const uint32_t u[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<AB16>(u[j]);
+            a0 = fmaf(f.x, f.x, a0);
+            a1 = fmaf(f.y, f.y, a1);
+          }
+        }
+        rqv = rsqrtf(a0 + a1 + 1e-6f);
+      }
       float ext[4] = {0.f, 0.f, 0.f, 0.f};
       if (!cols_above) tmem_ld64(lrow + T_R + T_RSTRIDE * pb + 64 * hp, v);
       if (hp == 0) tmem_ld4(lrow + T_R + T_RSTRIDE * pb + 128, ext);
@@ -534,7 +573,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
           }
         }
       }
-      if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 16);
+      if (c > 0) pipe_wait(&S.z_full[(c - 1) & 1], ((c - 1) >> 1) & 1, ab, err, 8);
       if (!cols_above) tmem_st32(lrow + T_P + 32 * hp, v);
       if (hp == 0) tmem_st1(lrow + T_P + 64, pack2<AB16>(-sp, -sp));
       tmem_st_wait();
@@ -542,16 +581,18 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       warp_arrive(&S.pready);
       // lambda / pos for the output group and the token_aux side output, while F2b runs
       if (hp == 0) {
+        // NORM: the gate logit and s_t were formed from the raw q; r_t scales both
         float lamv;
-        if (gate) lamv = sigmoidf_(ext[2] + ext[3] + gate_b);
+        if (gate) lamv = sigmoidf_(rqv * (ext[2] + ext[3]) + gate_b);
         else lamv = t < valid ? act_load<AB16>(a.lam, (sq.bos + t0 + t) * H + h) : 0.f;
         S.cf[pb][t] = lamv * ipos;
         if (NORM) S.rqo[pb][t] = rqv;
         warp_arrive(&S.cf_ready[pb]);
         if (a.token_aux && t < valid) {
           float2* aux = reinterpret_cast<float2*>(a.token_aux + ((sq.bos + t0 + t) * H + h) * 2);
-          *aux = make_float2(lamv, st);
+          *aux = make_float2(lamv, st * rqv);
         }
+        if (NORM && t < valid) a.norm_aux[((sq.bos + t0 + t) * H + h) * 2] = rqv;
       }
     }
   } else {
@@ -604,12 +645,15 @@ __global__ void __launch_bounds__(F_THREADS, 1)
         pipe_wait(&S.cprev_free, c & 1, ab, err, 64);
         store_row64<AB16>(cpan, r, v);
         fence_async_smem();
+        // cconv is one barrier whose phases are tested by parity: arrive only for a chunk that
+        // exists.  An arrival in the last chunk could complete a second phase before the MMA
+        // thread has tested the one for the last chunk's F2a, which then would read as pending.
+        warp_arrive(&S.cconv);
       } else if (a.final_cov) {
         float4* dst = reinterpret_cast<float4*>(a.final_cov + (st_base + r) * 128 + 64 * ho);
 #pragma unroll
         for (int i = 0; i < 16; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
-      warp_arrive(&S.cconv);
       // ---------------- q_clean of chunk c = q - (lambda / pos) Z
       // The Q tile of the stage was released after the chunk's last MMA; q is read again (from L2)
       // into the staging tile, once the previous bulk store has read that tile.
@@ -625,16 +669,16 @@ __global__ void __launch_bounds__(F_THREADS, 1)
       tmem_ld64(lrow + T_R + T_RSTRIDE * s + 64 * ho, v);
       tc_fence_before();
       warp_arrive(&S.z_free[s]);
-      pipe_wait(&S.cf_ready[s], (c >> 1) & 1, ab, err, 128);
-      const float cf = S.cf[s][r];
+      pipe_wait(&S.cf_ready[s], (c >> 1) & 1, ab, err, 0x200);
       const float rq = NORM ? S.rqo[s][r] : 1.f;
+      const float cf = NORM ? S.cf[s][r] * rq : S.cf[s][r];  // NORM: Z holds Z_true / r_t
       const uint32_t opan = sbase + F_OFF_O + (uint32_t)ho * F_QPANEL;
-      own_copy_wait(&S.qo_full, c & 1, ab, err, 128);  // q of this chunk, reloaded into the staging tile
+      own_copy_wait(&S.qo_full, c & 1, ab, err, 0x400);  // q of this chunk, reloaded into the staging tile
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         const uint32_t ad = opan + sw128(r, cc);
         uint4 qv = ld_shared_v4(ad);
-        if (NORM) {  // the raw q re-read from memory, normalised exactly as the aux warps did it
+        if (NORM) {  // the raw q re-read from memory, normalised and rounded as l2norm's output
           uint32_t u[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -704,7 +748,7 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
     tkn = tk;  // unused
   }
   int* err = reinterpret_cast<int*>(a.workspace);
-  if ((e = cudaMemsetAsync(err, 0, sizeof(int), a.stream)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(err, 0, 2 * sizeof(int), a.stream)) != cudaSuccess) return e;
   CleanArgs la = a;
   la.doc_order = nullptr;
   if (lpt_order_bytes(a.n_seqs, a.cu_seqlens != nullptr) > 0) {
