@@ -41,8 +41,9 @@ FWD_BYTES_PER_TH = 768      # q, k read + q_clean write (bf16)
 BWD_BYTES_PER_TH = 1280     # q, k, dq_clean read + dq, dk write (bf16)
 FLOP_PER_TH = 339968
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
-# kernel at c2; profiles/tc_fwd_kernel_c2.md and profiles/tc_bwd_kernel_c2.md give the command.
-NCU_TRAFFIC_C2 = {'fwd': 270.7e6 + 108.9e6, 'bwd': 2 * (207.7e6 + 102.5e6)}  # bwd: batch-4 capture x 2
+# kernel on the c2 shapes at batch 4, doubled for batch 8 (traffic grows with the (document, head)
+# count); profiles/tc_fwd_kernel_c2.md and profiles/tc_bwd_kernel_c2.md give the commands.
+NCU_TRAFFIC_C2 = {'fwd': 2 * (134.3e6 + 41.6e6), 'bwd': 2 * (207.7e6 + 102.5e6)}  # batch-4 captures x 2
 NCU_TRAFFIC_C4 = 272.7e6 + 213.9e6  # decode_kernel, profiles/decode_kernel_c4.md
 DECODE_BYTES_PER_TH = 2 * 128 * 128 * 4 + 2 * 128 * 4 + 4 * 128 * 2 + 2 * 2
 
