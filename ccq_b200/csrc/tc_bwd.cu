@@ -483,6 +483,16 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     tc_fence_before();
     warp_arrive(&S.tinit);
     float db_acc = 0.f;
+    // this token's (lambda, s) from the forward (and NORM: 1/|q|) are loaded one chunk ahead, so the
+    // load's latency is hidden behind a whole chunk period instead of sitting before E1; chunks after
+    // the first one processed (the document's last, possibly partial chunk) are always full
+    float2 ax_nx = make_float2(0.f, 0.f);
+    float rqn_nx = 0.f;
+    if (nchunks > 0 && t < sq.len - (nchunks - 1) * B_BT) {
+      const int64_t tok = sq.bos + (int64_t)(nchunks - 1) * B_BT + t;
+      ax_nx = *reinterpret_cast<const float2*>(a.token_aux_in + (tok * H + h) * 2);
+      if (NORM && !dside) rqn_nx = a.norm_aux_in[(tok * H + h) * 2];
+    }
 
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1, c = nchunks - 1 - i;
@@ -491,43 +501,25 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const uint32_t st = sbase + s * B_STAGE;
       const uint32_t rb = sR + s * 2048;              // this chunk's R buffer
       const bool tv = t < valid;
-      // this token's (lambda, s) from the forward, loaded early so its latency hides behind E0G
-      float2 ax = make_float2(0.f, 0.f);
-      if (tv) ax = *reinterpret_cast<const float2*>(a.token_aux_in + ((sq.bos + t0 + t) * H + h) * 2);
-      const float rqn = (NORM && tv && !dside) ? a.norm_aux_in[((sq.bos + t0 + t) * H + h) * 2] : 0.f;
+      const float2 ax = ax_nx;
+      const float rqn = rqn_nx;
+      if (i + 1 < nchunks) {
+        const int64_t tok = sq.bos + (int64_t)(t0 - B_BT) + t;
+        ax_nx = *reinterpret_cast<const float2*>(a.token_aux_in + (tok * H + h) * 2);
+        if (NORM && !dside) rqn_nx = a.norm_aux_in[(tok * H + h) * 2];
+      }
       pipe_wait(&S.m_ready[s], (i >> 1) & 1, ab, err, 32);  // long done; checked while B4 still runs
-      // ---------------- G (after this chunk) -> bf16 operand of B3
-      if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
-      tc_fence_after();
-      tmem_ld64(lrow + T_G + 64 * g, v);
-      store_panel_row<AB16>(sG + g * 16384, r, v);
-      fence_async_smem();
-      tc_fence_before();
-
-      // ---------------- E1: P2, tril(A), P4, dZ, R columns
-      pipe_wait(&S.da_full, i & 1, ab, err, 32);
-      tc_fence_after();
       const float lamv = ax.x, sv = sub_mean ? ax.y : 0.f;
       const float ipos = 1.f / position_of(t0 + t, a.position_offset);
       const float alpha = lamv * ipos;
-      tmem_ld32(lrow + T_DA + 32 * g, v);
       const float* mp = S.m_buf[s];
+
+      // ---------------- E1a: the part of E1 that does not need this chunk's scores, done while B1 runs:
+      // m_prev . dqc_t (z rows), dZ = -alpha dqc into the stage and the start values of ZQ (zero for
+      // the z rows, dq_clean for the dq rows; E2 of the previous chunk has read ZQ)
+      pipe_wait(&S.full[s], (i >> 1) & 1, ab, err, 32);  // this chunk's dQc / Q tiles
+      float wq_t = 0.f;
       if (dside) {
-        float wp = 0.f;
-        if (!cols_above) {
-          float tr[8];
-#pragma unroll
-          for (int k8 = 0; k8 < 8; ++k8) {
-            float x = 0.f;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int jj = 8 * u + k8;
-              x += (cols_below || 32 * g + jj <= t) ? v[jj] : 0.f;
-            }
-            tr[k8] = x;
-          }
-          wp = ((tr[0] + tr[1]) + (tr[2] + tr[3])) + ((tr[4] + tr[5]) + (tr[6] + tr[7]));
-        }
         if (sub_mean) {
           const float4* mp4 = reinterpret_cast<const float4*>(mp + 64 * g);
           float wq[4] = {0.f, 0.f, 0.f, 0.f};
@@ -541,7 +533,57 @@ __global__ void __launch_bounds__(B_THREADS, 1)
             wq[2] = fmaf(ma.z, f[2], fmaf(mb.z, f[6], wq[2]));
             wq[3] = fmaf(ma.w, f[3], fmaf(mb.w, f[7], wq[3]));
           }
-          wp += (wq[0] + wq[1]) + (wq[2] + wq[3]);
+          wq_t = (wq[0] + wq[1]) + (wq[2] + wq[3]);
+        }
+#pragma unroll
+        for (int cc = 0; cc < 64; ++cc) v[cc] = 0.f;
+      } else {
+        // dZ = -alpha dqc, packed.  These rows held the previous chunk's dq tile of this warp, staged
+        // for its bulk store: wait until that store has read them.
+        const float na = tv ? -alpha : 0.f;
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+        const uint32_t na2 = pack2<AB16>(na, na);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
+          st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), mul2<AB16>(d.x, na2), mul2<AB16>(d.y, na2),
+                       mul2<AB16>(d.z, na2), mul2<AB16>(d.w, na2));
+          unpack8<AB16>(d, v + 8 * cc);
+        }
+      }
+      // B2 accumulates onto ZQ: its dq rows start from dq_clean (fp32), its z rows from zero
+      tmem_st32(lrow + T_ZQ + 64 * g, v);
+      tmem_st32(lrow + T_ZQ + 64 * g + 32, v + 32);
+      tmem_st_wait();
+
+      // ---------------- G (after this chunk) -> bf16 operand of B3
+      if (i >= 1) pipe_wait(&S.g_full, (i - 1) & 1, ab, err, 16);
+      tc_fence_after();
+      tmem_ld64(lrow + T_G + 64 * g, v);
+      store_panel_row<AB16>(sG + g * 16384, r, v);
+      fence_async_smem();
+      tc_fence_before();
+
+      // ---------------- E1b: P2, tril(A), P4, R columns (needs [D ; A] of B1)
+      pipe_wait(&S.da_full, i & 1, ab, err, 32);
+      tc_fence_after();
+      tmem_ld32(lrow + T_DA + 32 * g, v);
+      if (dside) {
+        float wp = wq_t;
+        if (!cols_above) {
+          float tr[8];
+#pragma unroll
+          for (int k8 = 0; k8 < 8; ++k8) {
+            float x = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int jj = 8 * u + k8;
+              x += (cols_below || 32 * g + jj <= t) ? v[jj] : 0.f;
+            }
+            tr[k8] = x;
+          }
+          wp += ((tr[0] + tr[1]) + (tr[2] + tr[3])) + ((tr[4] + tr[5]) + (tr[6] + tr[7]));
         }
         S.wpart[g][t] = wp;
         bar_sync_quad<3, 64>(qd);
@@ -580,28 +622,8 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           st_shared_v4(sAP + sw128(t, 4 * g + q4), am[0], am[1], am[2], am[3]);
           st_shared_v4(sP4 + sw128(t, 4 * g + q4), p4[0], p4[1], p4[2], p4[3]);
         }
-        // dZ = -alpha dqc, packed.  These rows held the previous chunk's dq tile of this warp, staged
-        // for its bulk store: wait until that store has read them.
-        if (lane == 0) bulk_wait_read();
-        __syncwarp();
-        const uint32_t na2 = pack2<AB16>(na, na);
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint4 d = ld_shared_v4(st + g * B_QDPANEL + sw128(t, cc));
-          st_shared_v4(st + g * B_QDPANEL + 16384 + sw128(t, cc), mul2<AB16>(d.x, na2), mul2<AB16>(d.y, na2),
-                       mul2<AB16>(d.z, na2), mul2<AB16>(d.w, na2));
-          unpack8<AB16>(d, v + 8 * cc);
-        }
         if (g == 0) st_shared_u16(rb + sw128(2, t >> 3) + (t & 7) * 2, to16<AB16>(beta));
       }
-      if (dside) {
-#pragma unroll
-        for (int cc = 0; cc < 64; ++cc) v[cc] = 0.f;
-      }
-      // B2 accumulates onto ZQ: its dq rows start from dq_clean (fp32), its z rows from zero
-      tmem_st32(lrow + T_ZQ + 64 * g, v);
-      tmem_st32(lrow + T_ZQ + 64 * g + 32, v + 32);
-      tmem_st_wait();
       fence_async_smem();
 
       // ---------------- C_prev -> bf16 operand of B2
