@@ -43,7 +43,7 @@ FLOP_PER_TH = 339968
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
 # kernel on the c2 shapes at batch 4, doubled for batch 8 (traffic grows with the (document, head)
 # count); profiles/tc_fwd_kernel_c2.md and profiles/tc_bwd_kernel_c2.md give the commands.
-NCU_TRAFFIC_C2 = {'fwd': 2 * (134.3e6 + 41.6e6), 'bwd': 2 * (207.7e6 + 102.5e6)}  # batch-4 captures x 2
+NCU_TRAFFIC_C2 = {'fwd': 2 * (134.3e6 + 41.6e6), 'bwd': 2 * (207.8e6 + 100.8e6)}  # batch-4 captures x 2 (profiles/)
 NCU_TRAFFIC_C4 = 272.7e6 + 213.9e6  # decode_kernel, profiles/decode_kernel_c4.md
 DECODE_BYTES_PER_TH = 2 * 128 * 128 * 4 + 2 * 128 * 4 + 4 * 128 * 2 + 2 * 2
 
