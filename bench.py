@@ -575,13 +575,13 @@ def run_c2_l2norm(args, rank, world, device, hbm_peak, tf_peak):
         step_s = el / args.steps
         res[name] = {'ms_per_step': step_s * 1e3, 'value': B * T * world / step_s, 'unit': 'tokens/s'}
     # fused path, algorithmic bytes per token-head: fwd reads q, k and writes q_clean, k_norm (+16 B of
-    # per-token side outputs); bwd reads q, k_norm, dq_clean (+16 B), writes dq and dk_norm; the key
-    # gradient then reads dk_norm, the backbone's gradient and k_norm and writes dk
+    # per-token side outputs); bwd reads q, k_norm, dq_clean and the backbone's gradient on k_norm
+    # (+16 B) and writes dq and dk (the key gradient is mapped through the norm inside the kernel)
     th = B * T * H
-    step_bytes = (1040 + 1296 + 1032) * th
+    step_bytes = (1040 + 1552) * th
     ach = step_bytes / (res['fused']['ms_per_step'] * 1e-3) / 1e9
     res['fused']['roofline'] = {'bound': 'hbm', 'achieved': ach, 'peak': hbm_peak, 'unit': 'GB/s',
-                                'frac': ach / hbm_peak, 'bytes_per_token_head': 3368}
+                                'frac': ach / hbm_peak, 'bytes_per_token_head': 2592}
     res['workload'] = ('c2 shapes with raw (un-normalised) bf16 q, k ~ N(0,1), per-token lambda, gradients on '
                        'q_clean and on the normalised keys; through the autograd API')
     return res

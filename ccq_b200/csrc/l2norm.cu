@@ -5,9 +5,9 @@
 // ccq/ops/ccq_gla/fused_chunk.py:31-32):
 //   forward   r = 1 / sqrt(sum(x^2) + eps),  y = x * r        (fp32 math, y in the activation dtype)
 //   backward  dx = r * (dy - y * sum(dy * y))                 (y the stored, rounded output)
-// The tensor-core kernels fold the normalisation into their tile loads; these kernels serve the
-// exact fp32 / general-K path and the k side of the tensor-core backward, whose gradient on the
-// normalised keys (the operator's own plus the one arriving from the backbone) is mapped back here.
+// The tensor-core kernels fold the normalisation (and its backward) into their tiles; these kernels
+// serve the exact fp32 / general-K path, whose gradient on the normalised keys (the operator's own
+// plus the one arriving from the backbone) is mapped back here.
 //
 // One warp per row of K elements (K <= 256, K % 2 == 0); a row is a (token, head) vector.
 #include "args.h"

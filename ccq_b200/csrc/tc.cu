@@ -34,7 +34,8 @@ bool tc_supported(const CleanArgs& a, int op) {
   if (a.initial_cov && !aligned16(a.initial_cov)) return false;
   if (a.final_cov && !aligned16(a.final_cov)) return false;
   if (op == 1 && !(aligned16(a.dq_clean) && aligned16(a.dq) && aligned16(a.dk) &&
-                   aligned16(a.state_cov) && (a.dfinal_cov == nullptr || aligned16(a.dfinal_cov))))
+                   aligned16(a.state_cov) && (a.dfinal_cov == nullptr || aligned16(a.dfinal_cov)) &&
+                   (a.dk_ext == nullptr || aligned16(a.dk_ext))))
     return false;
   return device_major() == 10;
 }

@@ -24,8 +24,8 @@
 // aux warps rescale each chunk's Q rows in shared memory by the forward's 1/|q_t| (the same rounded
 // products the forward formed), and the dq epilogue maps the gradient on the normalised q back
 // through the normalisation, dq = (dq_hat - q_hat (q_hat . dq_hat)) / |q| (fla/modules/l2norm.py:49-72).
-// The gradient on the normalised keys is mapped back by a streaming kernel afterwards (l2norm.cu),
-// once the backbone's share of it has been added.
+// The gradient on the normalised keys, plus the backbone's share of it (an input), is mapped back
+// the same way in E3, against the normalised keys the stage's K tile still holds.
 //
 // Warp roles (384 threads): warp 0 TMA loads, warp 1 TMEM + MMA issue, warps 2-3 aux (partial-chunk
 // key zeroing and the running key sum m walked backwards), warps 4-11 epilogue.  The epilogue writes
@@ -780,6 +780,9 @@ __global__ void __launch_bounds__(B_THREADS, 1)
       const float carry = tmem_carry(lrow + T_CW);            // of dim 32qd + lane
       tc_fence_before();
       warp_arrive(&S.dk_read);
+      // NORM: dk on the normalised keys is staged in [tril(A) ; P2] (free from dk_full until the next
+      // chunk's E1) and mapped into the K tile below, which still holds this chunk's normalised keys
+      const uint32_t dkst = NORM ? sAP : st + B_OFF_K;
       {  // dk rows (tokens) written as 8 x 8 blocks transposed out of the fragment layout
         const int mi = lane >> 3, ri = lane & 7;  // this thread addresses row ri of matrix mi
 #pragma unroll
@@ -791,12 +794,67 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             const int k0 = 2 * h2, kk = k0 + (mi >> 1);      // matrices: (k0, dims +0), (k0, +8), (k0+1, +0), (k0+1, +8)
-            const uint32_t addr = st + B_OFF_K + (dd >> 6) * B_KPANEL + sw128(32 * g + 8 * kk + ri, (dd & 63) >> 3);
+            const uint32_t addr = dkst + (dd >> 6) * B_KPANEL + sw128(32 * g + 8 * kk + ri, (dd & 63) >> 3);
             stmatrix_x4_trans(addr, pack2<AB16>(f[4 * k0] + cu, f[4 * k0 + 1] + cu),
                               pack2<AB16>(f[4 * k0 + 2] + cl, f[4 * k0 + 3] + cl),
                               pack2<AB16>(f[4 * k0 + 4] + cu, f[4 * k0 + 5] + cu),
                               pack2<AB16>(f[4 * k0 + 6] + cl, f[4 * k0 + 7] + cl));
           }
+        }
+      }
+      if (NORM) {
+        // the gradient on the normalised keys mapped back through the normalisation (fla's l2norm
+        // backward, fla/modules/l2norm.py:49-72): dk = (s - k_hat (k_hat . s)) / |k| with
+        // s = dk_hat + the backbone's gradient on k_hat, rounded to 16 bits as autograd's sum of the
+        // two would be.  Four threads per token row, 32 dims (64 bytes) each; the result replaces
+        // k_hat in the K tile, which the TMA thread stores as dk.
+        const int row = et >> 2, qq = et & 3, pn = qq >> 1, c0 = 4 * (qq & 1);
+        const bool rv = row < valid;
+        const int64_t tok = sq.bos + (int64_t)t0 + row;
+        uint4 ev[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
+                       make_uint4(0u, 0u, 0u, 0u)};
+        if (rv && a.dk_ext) {
+          const uint4* ep = reinterpret_cast<const uint4*>((const uint8_t*)a.dk_ext + ((tok * H + h) * 128 + 32 * qq) * 2);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) ev[c] = ep[c];
+        }
+        const float rk = rv ? a.norm_aux_in[(tok * H + h) * 2 + 1] : 0.f;
+        bar_sync<1, 256>();  // every warp's block of dk_hat is staged
+        uint4 dv[4], kv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          dv[c] = ld_shared_v4(sAP + pn * B_KPANEL + sw128(row, c0 + c));
+          kv[c] = ld_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, c0 + c));
+        }
+        bar_sync<1, 256>();  // [tril(A) ; P2] is read: the next chunk's E1 may overwrite it
+        uint32_t sp[16];
+        float dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t dw[4] = {dv[c].x, dv[c].y, dv[c].z, dv[c].w};
+          const uint32_t ew[4] = {ev[c].x, ev[c].y, ev[c].z, ev[c].w};
+          const uint32_t kw[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 d2 = unpack2<AB16>(dw[j]), e2 = unpack2<AB16>(ew[j]), k2 = unpack2<AB16>(kw[j]);
+            sp[4 * c + j] = pack2<AB16>(d2.x + e2.x, d2.y + e2.y);
+            const float2 s2 = unpack2<AB16>(sp[4 * c + j]);
+            dot = fmaf(s2.x, k2.x, dot);
+            dot = fmaf(s2.y, k2.y, dot);
+          }
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t kw[4] = {kv[c].x, kv[c].y, kv[c].z, kv[c].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 s2 = unpack2<AB16>(sp[4 * c + j]), k2 = unpack2<AB16>(kw[j]);
+            o[j] = pack2<AB16>(rk * (s2.x - k2.x * dot), rk * (s2.y - k2.y * dot));
+          }
+          st_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, c0 + c), o[0], o[1], o[2], o[3]);
         }
       }
       if (valid < B_BT) {  // a document's last, partial chunk: plain stores of its valid rows
@@ -893,11 +951,6 @@ cudaError_t launch(const CleanArgs& a, int* launches) {
     gate_sum_kernel<<<a.H, 128, 0, a.stream>>>(part, a.n_seqs, a.H, a.dgate_w, a.dgate_b);
     *launches += 1;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
-  if (NORM) {  // dk on the normalised keys (+ the backbone's share) -> dk on the raw keys, in place
-    e = l2norm_rows_bwd(a.dtype, a.dk, a.dk_ext, a.k, a.norm_aux_in, 1, rows * a.H, 128, a.stream);
-    *launches += 1;
-    if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
