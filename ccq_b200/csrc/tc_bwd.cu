@@ -64,7 +64,7 @@ struct BwdSmall {
   float w[64], ds[64], dpre[64];
   float qdot[2][64];  // NORM: [column half][token] partial q_hat . dq_hat
   uint64_t full[2], kready[2], empty[2], m_ready[2], m_free[2];
-  uint64_t tinit, da_full, c_full, cconv, g_full, zq_full, dk_full, dk_read, cw_done, mma_done;
+  uint64_t tinit, da_full, c_full, cconv, g_full, zq_full, dk_full, dk_read, cw_done, mma_done, ap_free;
   float db;
   uint32_t tmem_base;
   int abort;
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
     uint64_t* ones[] = {&S.da_full, &S.c_full, &S.g_full, &S.zq_full, &S.dk_full, &S.cw_done,
                         &S.mma_done};
     for (uint64_t* b : ones) mbar_init(b, 1);
-    uint64_t* epis[] = {&S.tinit, &S.cconv, &S.dk_read};
+    uint64_t* epis[] = {&S.tinit, &S.cconv, &S.dk_read, &S.ap_free};
     for (uint64_t* b : epis) mbar_init(b, EPI_WARPS);
     S.abort = 0;
     S.db = 0.f;
@@ -567,6 +567,7 @@ __global__ void __launch_bounds__(B_THREADS, 1)
 
       // ---------------- E1b: P2, tril(A), P4, R columns (needs [D ; A] of B1)
       pipe_wait(&S.da_full, i & 1, ab, err, 32);
+      if (NORM && i >= 1) pipe_wait(&S.ap_free, (i - 1) & 1, ab, err, 32);  // E3 of the last chunk read it
       tc_fence_after();
       tmem_ld32(lrow + T_DA + 32 * g, v);
       if (dside) {
@@ -819,14 +820,15 @@ __global__ void __launch_bounds__(B_THREADS, 1)
           for (int c = 0; c < 4; ++c) ev[c] = ep[c];
         }
         const float rk = rv ? a.norm_aux_in[(tok * H + h) * 2 + 1] : 0.f;
-        bar_sync<1, 256>();  // every warp's block of dk_hat is staged
+        if (g == 0) bar_sync<9, 128>();  // the four warps of this token half have staged their blocks
+        else bar_sync<10, 128>();
         uint4 dv[4], kv[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           dv[c] = ld_shared_v4(sAP + pn * B_KPANEL + sw128(row, c0 + c));
           kv[c] = ld_shared_v4(st + B_OFF_K + pn * B_KPANEL + sw128(row, c0 + c));
         }
-        bar_sync<1, 256>();  // [tril(A) ; P2] is read: the next chunk's E1 may overwrite it
+        warp_arrive(&S.ap_free);  // [tril(A) ; P2] is read: the next chunk's E1b may overwrite it
         uint32_t sp[16];
         float dot = 0.f;
 #pragma unroll
