@@ -37,7 +37,7 @@ def _np(t):
     return None if t is None else t.detach().double().cpu().numpy()
 
 
-def _run(case, dtype, seed=3):
+def _run(case, dtype, seed=3, key_grad=True):
     import ccq_b200
     c = CASES[case]
     g = torch.Generator(device='cuda').manual_seed(seed)
@@ -51,6 +51,8 @@ def _run(case, dtype, seed=3):
     lam0 = torch.rand(B, T, H, generator=g, device='cuda')
     dqc = torch.randn(B, T, H, K, generator=g, device='cuda').to(dtype)
     dkn = torch.randn(B, T, H, K, generator=g, device='cuda').to(dtype)
+    if not key_grad:  # nothing downstream reads the normalised keys: no gradient arrives on them
+        dkn = torch.zeros_like(dkn)
     h00 = m00 = dfc = dfm = None
     if c['states']:
         kk = torch.nn.functional.normalize(torch.randn(N, 16, H, K, generator=g, device='cuda'), dim=-1)
@@ -68,7 +70,9 @@ def _run(case, dtype, seed=3):
                                                           initial_mean_state=m0, output_final_state=True,
                                                           subtract_mean=c['sm'], cu_seqlens=cu)
     path = ccq_b200.last_path()
-    loss = (qc.float() * dqc.float()).sum() + (kn.float() * dkn.float()).sum()
+    loss = (qc.float() * dqc.float()).sum()
+    if key_grad:
+        loss = loss + (kn.float() * dkn.float()).sum()
     if dfc is not None:
         loss = loss + (fc * dfc).sum()
     if dfm is not None:
@@ -114,6 +118,18 @@ def test_l2norm_fused_against_oracle(case, dtype):
         else:
             e = float(np.abs(a - ref[name]).max())
             assert e <= 2e-2, f'{case}.{name}: max-abs err {e:.3e}'
+
+
+@pytest.mark.parametrize('case', ['dense', 'varlen_states'])
+def test_l2norm_without_key_gradient(case):
+    """The normalised keys feed nothing downstream, so the backward gets no gradient on them (a null
+    pointer through the C ABI): the key gradient is the operator's own, mapped through the norm."""
+    out, inp, path = _run(case, torch.bfloat16, seed=11, key_grad=False)
+    assert path == 'tcgen05'
+    ref = _oracle(case, inp, torch.bfloat16)
+    for name in ('q_clean', 'dq', 'dk', 'dlam'):
+        e = float(np.abs(_np(out[name]) - ref[name]).max())
+        assert e <= 2e-2, f'{case}.{name}: max-abs err {e:.3e}'
 
 
 @pytest.mark.parametrize('case', ['dense', 'varlen_states'])
