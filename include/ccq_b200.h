@@ -173,7 +173,9 @@ int ccq_clean_l2norm_fwd(int dtype, int B, int T, int H, int K,
  * FusedCCQCleanRead.backward, fused_read.py:496-514), including autograd's sum of the two
  * gradients on the normalised keys (the operator's and the backbone's).
  *   q: the raw queries; k_norm: the forward's k_norm output; norm_aux: the forward's norm_aux.
- *   dk_norm: optional gradient arriving on k_norm from the rest of the model (NULL = none).
+ *   dk_norm: optional gradient arriving on k_norm from the rest of the model (NULL = none); the
+ *     tensor-core path adds it inside its kernel and needs it 16-byte aligned (otherwise the call
+ *     takes the exact path, as for the other tensors).
  *   dq, dk: outputs, gradients on the raw q and k.  Everything else as ccq_clean_bwd.
  */
 int ccq_clean_l2norm_bwd(int dtype, int B, int T, int H, int K,
